@@ -1,0 +1,115 @@
+/*
+ * mfa.h — C ABI of libmfa.so, the B200 (sm_100a) flash-attention forward engine.
+ *
+ * This library replaces the kernel-tier layer that sits under the reference's boundary
+ * function `flash_attn_forward` (metal_flash_attn/_kernel.py:1052-1153). That function picks
+ * one of the Metal tiers v0/v1/v2/v2r (metal_flash_attn/_kernel.py:974-985) and launches it
+ * through torch.mps.compile_shader (e.g. metal_flash_attn/_kernel.py:1309-1312, 1416-1419).
+ * Here the same boundary is one C call, `mfa_fwd`, with plain device pointers, element strides
+ * and scalars; no torch types cross it.
+ *
+ * Semantics (identical to the reference's chunked-fp32 torch tier,
+ * metal_flash_attn/_kernel.py:1165-1208):
+ *   s  = (q . k) * scale
+ *   s  = softcap * tanh(s / softcap)              if softcap > 0
+ *   s -= alibi[b*Hq + h] * |center - j|           if alibi != NULL
+ *   masked (-inf) unless kmin <= j < kmax, with center = i + (Lk - Lq) (bottom-right),
+ *     causal: j <= center; win_left >= 0: j >= center - win_left;
+ *     win_right >= 0: j <= center + win_right
+ *   o  = softmax(s) @ v ; a row with no unmasked key is 0 (nan_to_num, _kernel.py:1206)
+ * GQA/MQA: query head h reads kv head h / (Hq / Hkv).
+ *
+ * Ownership: the caller owns every buffer. Launches are asynchronous on the caller's stream.
+ * No C++ exception crosses the ABI; every entry returns an mfa_status.
+ * The library is reentrant and safe to call from several host threads.
+ */
+#ifndef MFA_H_
+#define MFA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MFA_ABI_VERSION 1
+
+/* Status codes. The Python layer maps them to the reference's exception types. */
+enum mfa_status {
+  MFA_OK = 0,
+  MFA_ERR_INVALID = 1,        /* bad argument (ValueError in the reference) */
+  MFA_ERR_UNSUPPORTED = 2,    /* feature or shape not supported (NotImplementedError) */
+  MFA_ERR_CUDA = 3,           /* CUDA runtime / driver failure (RuntimeError) */
+  MFA_ERR_TIMEOUT = 4,        /* a bounded in-kernel wait expired; output is invalid */
+  MFA_ERR_NO_DEVICE = 5,      /* no usable sm_100 device for the requested kernel */
+  MFA_ERR_FAULT_INJECTED = 6  /* host-side fault injection (MFA_FAULT env) fired */
+};
+
+enum mfa_dtype { MFA_FP16 = 0, MFA_BF16 = 1, MFA_FP32 = 2 };
+
+/* Kernel choice. AUTO picks TCGEN05 when eligible (fp16/bf16, D % 8 == 0, 16-byte aligned
+ * strides and pointers, sm_100 device), else SIMT. */
+enum mfa_kernel { MFA_KERNEL_AUTO = 0, MFA_KERNEL_TCGEN05 = 1, MFA_KERNEL_SIMT = 2 };
+
+typedef struct mfa_fwd_params {
+  const void* q;  /* [B, Lq, Hq, D] logical; any (batch, seq, head) strides, last dim stride 1 */
+  const void* k;  /* [B, Lk, Hkv, D] */
+  const void* v;  /* [B, Lk, Hkv, D] */
+  void* o;        /* [B, Lq, Hq, D] in o_dtype */
+  float* lse;     /* optional [B, Hq, Lq] natural-log sum-exp of each row (-inf if empty) */
+  int64_t q_stride[3]; /* element strides: batch, seq, head */
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int64_t o_stride[3];
+  int64_t lse_stride[2]; /* batch, head; the row stride is 1 */
+  int32_t B, Hq, Hkv, Lq, Lk, D;
+  /* varlen: device int32 [B+1] cumulative lengths, or NULL for dense. With varlen the batch
+   * strides are ignored, rows are absolute token indices, Lq/Lk hold the total token counts
+   * (total_q, total_k) and max_lq must be >= every per-sequence query length. */
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  int32_t max_lq, max_lk;
+  float scale;
+  float softcap;       /* 0 disables */
+  int32_t causal;      /* bottom-right aligned */
+  int32_t win_left;    /* -1 = unbounded */
+  int32_t win_right;   /* -1 = unbounded */
+  const float* alibi;  /* optional device fp32 [B*Hq] slopes */
+  int32_t dtype;       /* mfa_dtype of q/k/v */
+  int32_t o_dtype;     /* mfa_dtype of o; -1 = same as dtype */
+  /* split-KV: local key j is global key j + k_pos_offset; lk_total is the global key count
+   * used for the bottom-right centre (0 = use Lk). */
+  int32_t k_pos_offset;
+  int32_t lk_total;
+  int32_t kernel;      /* mfa_kernel */
+  int32_t* err;        /* optional device int; a kernel that times out stores MFA_ERR_TIMEOUT */
+} mfa_fwd_params;
+
+/* Attention forward. Replaces the tier dispatch under flash_attn_forward
+ * (metal_flash_attn/_kernel.py:1052-1153) and every Metal launcher it calls
+ * (_kernel.py:1288-1420). Returns MFA_OK or an error; a launch error is reported here,
+ * a kernel-side timeout through p->err. */
+int mfa_fwd(const mfa_fwd_params* p, void* cuda_stream);
+
+/* Which kernel mfa_fwd would run for these params (mfa_kernel value, never AUTO), or a
+ * negative mfa_status if the call would be rejected. Replaces the label logic of the
+ * reference's trace (_effective_kernel_label, metal_flash_attn/_kernel.py:995-1019). */
+int mfa_select_kernel(const mfa_fwd_params* p);
+
+/* Log-sum-exp merge of n partial results over disjoint key sets (split-KV). Partial g has
+ * o_part[g] fp32 [rows, H, D] (row stride H*D, head stride D) normalised by its own sum, and
+ * lse_part[g] fp32 [H, rows]. Writes o (o_dtype, same layout) and optionally lse [H, rows].
+ * No counterpart in the reference (its tiers never split keys); the merge restates
+ * lse = log sum_g exp(lse_g), o = sum_g exp(lse_g - lse) o_g. */
+int mfa_lse_combine(const float* const* o_part, const float* const* lse_part, int32_t n,
+                    int32_t rows, int32_t H, int32_t D, void* o, int32_t o_dtype,
+                    float* lse, void* cuda_stream);
+
+const char* mfa_status_string(int status);
+int mfa_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MFA_H_ */

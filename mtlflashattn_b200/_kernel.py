@@ -1,0 +1,292 @@
+"""The boundary: ``flash_attn_forward`` and the launch helpers under the public API.
+
+``flash_attn_forward`` keeps the signature, argument meaning, return layout and errors of the
+reference's boundary function (metal_flash_attn/_kernel.py:1052-1153): heads-second
+``[B, H, L, D]`` tensors of any strides in, a new contiguous ``[B, Hq, Lq, D]`` tensor in
+``q.dtype`` out. Underneath, the reference's Metal tier dispatch is replaced by one call into
+libmfa.so (include/mfa.h), which runs either the tcgen05 tensor-core kernel or the fp32
+CUDA-core kernel. Tensors cross that boundary only as pointers, strides and sizes; no layout
+copy is made for strided views.
+
+Tier names. ``MTLFLASHATTN_KERNEL`` accepts ``auto`` (default), ``tcgen05`` and ``simt``, and,
+for drop-in compatibility, the reference's tier names: ``v1``, ``v2``, ``v2_bf16`` map to
+``tcgen05``; ``v0`` and ``v2_fp32`` map to ``simt``; ``v2_dtype`` picks by dtype. A forced tier
+that cannot run the input raises RuntimeError, as in the reference (_kernel.py:1083-1139).
+The reference's ``torch`` tier is not part of this engine: that chunked-fp32 algorithm lives in
+``oracle/`` as the test checker only, and selecting it here raises RuntimeError.
+"""
+from __future__ import annotations
+
+import atexit
+import os
+import sys
+from collections import namedtuple
+
+import torch
+
+from . import _lib
+
+MAX_HEAD_DIM = 128
+
+# Bias/masking knobs, as in the reference (_kernel.py:20-24): softcap (0 = off),
+# window_left/window_right (-1 = open), alibi: [B*Hq] fp32 slopes already broadcast, or None.
+_BiasParams = namedtuple("_BiasParams", "softcap window_left window_right alibi")
+
+_DTYPES = {torch.float16: _lib.FP16, torch.bfloat16: _lib.BF16, torch.float32: _lib.FP32}
+
+_TIER_ALIASES = {
+    "auto": "auto", "cuda": "auto",
+    "tcgen05": "tcgen05", "tc": "tcgen05", "v1": "tcgen05", "v2": "tcgen05",
+    "v2_bf16": "tcgen05",
+    "simt": "simt", "v0": "simt", "v2_fp32": "simt",
+    "v2_dtype": "dtype", "v2_typed": "dtype",
+}
+
+
+def _tier_mode(dtype) -> int:
+    raw = os.environ.get("MTLFLASHATTN_KERNEL", "auto").lower()
+    if raw in ("torch", "pytorch"):
+        raise RuntimeError(
+            "mtlflashattn_b200: the chunked-fp32 torch tier is not part of this engine "
+            "(it is the test oracle); use MTLFLASHATTN_KERNEL=auto|tcgen05|simt"
+        )
+    mode = _TIER_ALIASES.get(raw)
+    if mode is None:
+        raise RuntimeError(f"mtlflashattn_b200: unknown MTLFLASHATTN_KERNEL={raw!r}")
+    if mode == "dtype":
+        mode = "simt" if dtype == torch.float32 else "tcgen05"
+    return {"auto": _lib.KERNEL_AUTO, "tcgen05": _lib.KERNEL_TCGEN05,
+            "simt": _lib.KERNEL_SIMT}[mode]
+
+
+# ------------------------------------------------------------------------------------ trace
+_trace = {}  # (dtype, D, Lq, Lk, causal, label) -> call count
+
+
+def _trace_enabled():
+    return os.environ.get("MTLFLASHATTN_TRACE", "").lower() in ("1", "on", "true", "yes")
+
+
+def _record_trace(dtype, D, Lq, Lk, causal, label):
+    """Count one call per (dtype, D, Lq, Lk, causal, kernel); never raises
+    (reference: _kernel.py:1022-1029)."""
+    try:
+        key = (str(dtype).replace("torch.", ""), int(D), int(Lq), int(Lk), bool(causal), label)
+        _trace[key] = _trace.get(key, 0) + 1
+    except Exception:
+        pass
+
+
+def _trace_summary_lines():
+    if not _trace:
+        return []
+    total = sum(_trace.values())
+    lines = [f"[MTLFLASHATTN_TRACE] {total} attention call(s), "
+             f"{len(_trace)} distinct shape/kernel combos:"]
+    for (dt, D, Lq, Lk, causal, label), n in sorted(_trace.items(), key=lambda kv: (-kv[1], kv[0])):
+        lines.append(f"  calls={n:<6} {dt:<9} D={D:<4} Lq={Lq:<6} Lk={Lk:<6} "
+                     f"causal={'T' if causal else 'F'}  -> {label}")
+    return lines
+
+
+@atexit.register
+def _trace_atexit():
+    if _trace_enabled() and _trace:
+        print("\n".join(_trace_summary_lines()), file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------------ device error word
+_err_words = {}
+
+
+def _err_word(device):
+    t = _err_words.get(device)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _err_words[device] = t
+    return t
+
+
+def check_device_errors(device=None):
+    """Synchronise and raise if any kernel on ``device`` reported a bounded-wait timeout."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    t = _err_words.get(dev)
+    if t is None:
+        return
+    torch.cuda.synchronize(dev)
+    v = int(t.item())
+    if v != 0:
+        t.zero_()
+        raise _lib.MfaError(v, "a kernel gave up on a bounded wait; its output is invalid")
+
+
+def _sync_check_enabled():
+    return os.environ.get("MTLFLASHATTN_SYNC_CHECK", "").lower() in ("1", "on", "true", "yes")
+
+
+# --------------------------------------------------------------------------------- launch
+def _broadcast_alibi_slopes(alibi_slopes, B, Hq, device):
+    """Flatten slopes ``[Hq]`` or ``[B, Hq]`` to contiguous fp32 ``[B*Hq]``
+    (reference: _kernel.py:1275-1285)."""
+    s = alibi_slopes.to(device=device, dtype=torch.float32)
+    if s.dim() == 1 and s.shape[0] == Hq:
+        s = s.unsqueeze(0).expand(B, Hq)
+    elif not (s.dim() == 2 and tuple(s.shape) == (B, Hq)):
+        raise ValueError(
+            f"mtlflashattn_b200: alibi_slopes must be [Hq={Hq}] or [B={B}, Hq={Hq}], "
+            f"got {tuple(s.shape)}"
+        )
+    return s.reshape(-1).contiguous()
+
+
+def _last_dim_contig(t):
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+def _raise_status(rc, what):
+    if rc == _lib.ERR_INVALID:
+        raise ValueError(f"mtlflashattn_b200: {what}: {_lib.status_string(rc)}")
+    if rc == _lib.ERR_UNSUPPORTED:
+        raise NotImplementedError(f"mtlflashattn_b200: {what}: {_lib.status_string(rc)}")
+    raise _lib.MfaError(rc, what)
+
+
+def _params(q, k, v, o, *, B, Hq, Hkv, Lq, Lk, D, q_st, k_st, v_st, o_st, scale, causal,
+            bias: _BiasParams, kernel, lse=None, lse_st=(0, 0), cu_q=None, cu_k=None,
+            max_lq=0, max_lk=0, k_pos_offset=0, lk_total=0):
+    p = _lib.MfaFwdParams()
+    p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
+    p.lse = lse.data_ptr() if lse is not None else None
+    p.q_stride[:] = q_st
+    p.k_stride[:] = k_st
+    p.v_stride[:] = v_st
+    p.o_stride[:] = o_st
+    p.lse_stride[:] = lse_st
+    p.B, p.Hq, p.Hkv, p.Lq, p.Lk, p.D = B, Hq, Hkv, Lq, Lk, D
+    p.cu_q = cu_q.data_ptr() if cu_q is not None else None
+    p.cu_k = cu_k.data_ptr() if cu_k is not None else None
+    p.max_lq, p.max_lk = max_lq, max_lk
+    p.scale = float(scale)
+    p.softcap = float(bias.softcap)
+    p.causal = 1 if causal else 0
+    p.win_left, p.win_right = int(bias.window_left), int(bias.window_right)
+    p.alibi = bias.alibi.data_ptr() if bias.alibi is not None else None
+    p.dtype = _DTYPES[q.dtype]
+    p.o_dtype = _DTYPES[o.dtype]
+    p.k_pos_offset = int(k_pos_offset)
+    p.lk_total = int(lk_total)
+    p.kernel = kernel
+    p.err = _err_word(q.device).data_ptr()
+    return p
+
+
+def _run(p, q, what, causal, trace_shape):
+    with torch.cuda.device(q.device):
+        if _trace_enabled():
+            sel = _lib.select_kernel(p)
+            label = "cuda/" + _lib.KERNEL_NAMES.get(sel, "rejected")
+            _record_trace(q.dtype, trace_shape[0], trace_shape[1], trace_shape[2], causal, label)
+        rc = _lib.fwd(p, torch.cuda.current_stream(q.device).cuda_stream)
+        if rc != _lib.OK:
+            if rc == _lib.ERR_UNSUPPORTED and p.kernel != _lib.KERNEL_AUTO:
+                raise RuntimeError(
+                    f"mtlflashattn_b200: {_lib.KERNEL_NAMES.get(p.kernel)} kernel forced but "
+                    f"ineligible (dtype={q.dtype}, D={p.D}; needs fp16/bf16, D%8==0, "
+                    f"16-byte aligned strides, sm_100 device)"
+                )
+            _raise_status(rc, what)
+    if _sync_check_enabled():
+        check_device_errors(q.device)
+
+
+def _check_tensors(q, k, v):
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise RuntimeError("mtlflashattn_b200 requires CUDA tensors (B200 / sm_100a)")
+    if k.device != q.device or v.device != q.device:
+        raise ValueError("mtlflashattn_b200: q/k/v must be on the same device")
+    if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise NotImplementedError(f"mtlflashattn_b200: dtype {q.dtype} (q/k/v must match, fp16/bf16/fp32)")
+
+
+def forward_bshd(q, k, v, out, scale, causal, bias: _BiasParams, lse=None, k_pos_offset=0,
+                 lk_total=0):
+    """Attention on heads-third ``[B, L, H, D]`` tensors of any strides, writing into ``out``
+    (``[B, Lq, Hq, D]``, any strides, fp16/bf16/fp32). ``lse`` is an optional fp32
+    ``[B, Hq, Lq]`` tensor. Launches exactly one kernel; no layout copies."""
+    _check_tensors(q, k, v)
+    q, k, v = _last_dim_contig(q), _last_dim_contig(k), _last_dim_contig(v)
+    B, Lq, Hq, D = q.shape
+    Lk, Hkv = k.shape[1], k.shape[2]
+    if Hkv == 0 or Hq % Hkv != 0:
+        raise ValueError(f"mtlflashattn_b200: num_heads_kv ({Hkv}) must divide num_heads_q ({Hq})")
+    if D > MAX_HEAD_DIM:
+        raise NotImplementedError(f"mtlflashattn_b200: head_dim {D} > {MAX_HEAD_DIM}")
+    if out.stride(-1) != 1:
+        raise ValueError("mtlflashattn_b200: out must have a contiguous last dimension")
+    p = _params(q, k, v, out, B=B, Hq=Hq, Hkv=Hkv, Lq=Lq, Lk=Lk, D=D,
+                q_st=(q.stride(0), q.stride(1), q.stride(2)),
+                k_st=(k.stride(0), k.stride(1), k.stride(2)),
+                v_st=(v.stride(0), v.stride(1), v.stride(2)),
+                o_st=(out.stride(0), out.stride(1), out.stride(2)),
+                scale=scale, causal=causal, bias=bias, kernel=_tier_mode(q.dtype),
+                lse=lse, lse_st=((lse.stride(0), lse.stride(1)) if lse is not None else (0, 0)),
+                k_pos_offset=k_pos_offset, lk_total=lk_total)
+    _run(p, q, "flash_attn_forward", causal, (D, Lq, Lk))
+    return out
+
+
+def forward_varlen(q, k, v, out, cu_q, cu_k, max_lq, max_lk, scale, causal, bias: _BiasParams,
+                   lse=None):
+    """Packed varlen attention in ONE launch: q ``[total_q, Hq, D]``, k/v ``[total_k, Hkv, D]``,
+    device int32 ``cu_q``/``cu_k`` ``[batch+1]``; ``bias.alibi`` is ``[batch*Hq]`` or None.
+    ``lse`` is an optional fp32 ``[Hq, total_q]`` tensor."""
+    _check_tensors(q, k, v)
+    q, k, v = _last_dim_contig(q), _last_dim_contig(k), _last_dim_contig(v)
+    total_q, Hq, D = q.shape
+    total_k, Hkv = k.shape[0], k.shape[1]
+    batch = cu_q.shape[0] - 1
+    p = _params(q, k, v, out, B=batch, Hq=Hq, Hkv=Hkv, Lq=total_q, Lk=total_k, D=D,
+                q_st=(0, q.stride(0), q.stride(1)), k_st=(0, k.stride(0), k.stride(1)),
+                v_st=(0, v.stride(0), v.stride(1)), o_st=(0, out.stride(0), out.stride(1)),
+                scale=scale, causal=causal, bias=bias, kernel=_tier_mode(q.dtype),
+                lse=lse, lse_st=((0, lse.stride(0)) if lse is not None else (0, 0)),
+                cu_q=cu_q, cu_k=cu_k, max_lq=max_lq, max_lk=max_lk)
+    _run(p, q, "flash_attn_varlen_func", causal, (D, max_lq, max_lk))
+    return out
+
+
+def flash_attn_forward(q, k, v, scale, causal, softcap=0.0, window_left=-1, window_right=-1,
+                       alibi_slopes=None):
+    """q: [B,Hq,Lq,D], k/v: [B,Hkv,Lk,D] (heads-second, any strides).
+
+    Returns [B,Hq,Lq,D] contiguous, in q.dtype (reference: _kernel.py:1052-1153).
+    """
+    if softcap < 0:
+        raise ValueError("mtlflashattn_b200: softcap must be >= 0 (0 disables capping)")
+    _check_tensors(q, k, v)
+    B, Hq, Lq, D = q.shape
+    alibi = (_broadcast_alibi_slopes(alibi_slopes, B, Hq, q.device)
+             if alibi_slopes is not None else None)
+    bias = _BiasParams(softcap, window_left, window_right, alibi)
+    out = torch.empty(B, Hq, Lq, D, device=q.device, dtype=q.dtype)
+    forward_bshd(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), out.transpose(1, 2),
+                 scale, causal, bias)
+    return out
+
+
+def _select_tier(q, k, v):
+    """Kernel ``auto`` would run for heads-second tensors: 'tcgen05', 'simt' or 'rejected'."""
+    try:
+        qb, kb, vb = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+        B, Lq, Hq, D = qb.shape
+        p = _params(qb, kb, vb, qb, B=B, Hq=Hq, Hkv=kb.shape[2], Lq=Lq, Lk=kb.shape[1], D=D,
+                    q_st=(qb.stride(0), qb.stride(1), qb.stride(2)),
+                    k_st=(kb.stride(0), kb.stride(1), kb.stride(2)),
+                    v_st=(vb.stride(0), vb.stride(1), vb.stride(2)),
+                    o_st=(qb.stride(0), qb.stride(1), qb.stride(2)),
+                    scale=1.0, causal=False, bias=_BiasParams(0.0, -1, -1, None),
+                    kernel=_lib.KERNEL_AUTO)
+        with torch.cuda.device(q.device):
+            return _lib.KERNEL_NAMES.get(_lib.select_kernel(p), "rejected")
+    except Exception:
+        return "rejected"

@@ -1,0 +1,152 @@
+"""ctypes binding of libmfa.so (C ABI declared in include/mfa.h).
+
+The shared library is built in-tree by ``mtlflashattn_b200.build`` and loaded from this
+package's directory. Nothing here falls back to another implementation: if the library is
+missing or a call fails, an exception is raised.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmfa.so")
+
+MFA_ABI_VERSION = 1
+
+# mfa_status
+OK = 0
+ERR_INVALID = 1
+ERR_UNSUPPORTED = 2
+ERR_CUDA = 3
+ERR_TIMEOUT = 4
+ERR_NO_DEVICE = 5
+ERR_FAULT_INJECTED = 6
+
+# mfa_dtype
+FP16, BF16, FP32 = 0, 1, 2
+
+# mfa_kernel
+KERNEL_AUTO, KERNEL_TCGEN05, KERNEL_SIMT = 0, 1, 2
+KERNEL_NAMES = {KERNEL_TCGEN05: "tcgen05", KERNEL_SIMT: "simt"}
+
+# Every symbol include/mfa.h declares.
+EXPORTED_SYMBOLS = (
+    "mfa_fwd",
+    "mfa_select_kernel",
+    "mfa_lse_combine",
+    "mfa_status_string",
+    "mfa_abi_version",
+)
+
+
+class MfaFwdParams(ctypes.Structure):
+    """Mirror of ``struct mfa_fwd_params`` (include/mfa.h)."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("o", ctypes.c_void_p),
+        ("lse", ctypes.c_void_p),
+        ("q_stride", ctypes.c_int64 * 3),
+        ("k_stride", ctypes.c_int64 * 3),
+        ("v_stride", ctypes.c_int64 * 3),
+        ("o_stride", ctypes.c_int64 * 3),
+        ("lse_stride", ctypes.c_int64 * 2),
+        ("B", ctypes.c_int32),
+        ("Hq", ctypes.c_int32),
+        ("Hkv", ctypes.c_int32),
+        ("Lq", ctypes.c_int32),
+        ("Lk", ctypes.c_int32),
+        ("D", ctypes.c_int32),
+        ("cu_q", ctypes.c_void_p),
+        ("cu_k", ctypes.c_void_p),
+        ("max_lq", ctypes.c_int32),
+        ("max_lk", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("softcap", ctypes.c_float),
+        ("causal", ctypes.c_int32),
+        ("win_left", ctypes.c_int32),
+        ("win_right", ctypes.c_int32),
+        ("alibi", ctypes.c_void_p),
+        ("dtype", ctypes.c_int32),
+        ("o_dtype", ctypes.c_int32),
+        ("k_pos_offset", ctypes.c_int32),
+        ("lk_total", ctypes.c_int32),
+        ("kernel", ctypes.c_int32),
+        ("err", ctypes.c_void_p),
+    ]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+class MfaError(RuntimeError):
+    """A libmfa call returned a non-OK status."""
+
+    def __init__(self, status: int, what: str = ""):
+        self.status = status
+        msg = f"libmfa: {status_string(status)} (status {status})"
+        if what:
+            msg = f"{msg}: {what}"
+        super().__init__(msg)
+
+
+def load(path: str | None = None) -> ctypes.CDLL:
+    """Load libmfa.so (once) and declare the C signatures. Raises if it is absent."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise RuntimeError(
+                f"libmfa.so not found at {p}; build it with `python -m mtlflashattn_b200.build`"
+            )
+        lib = ctypes.CDLL(p)
+        lib.mfa_fwd.argtypes = [ctypes.POINTER(MfaFwdParams), ctypes.c_void_p]
+        lib.mfa_fwd.restype = ctypes.c_int
+        lib.mfa_select_kernel.argtypes = [ctypes.POINTER(MfaFwdParams)]
+        lib.mfa_select_kernel.restype = ctypes.c_int
+        lib.mfa_lse_combine.argtypes = [
+            ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32,
+            ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int32,
+            ctypes.c_void_p, ctypes.c_void_p,
+        ]
+        lib.mfa_lse_combine.restype = ctypes.c_int
+        lib.mfa_status_string.argtypes = [ctypes.c_int]
+        lib.mfa_status_string.restype = ctypes.c_char_p
+        lib.mfa_abi_version.argtypes = []
+        lib.mfa_abi_version.restype = ctypes.c_int
+        if lib.mfa_abi_version() != MFA_ABI_VERSION:
+            raise RuntimeError(
+                f"libmfa ABI version {lib.mfa_abi_version()} != expected {MFA_ABI_VERSION}"
+            )
+        _lib = lib
+        return lib
+
+
+def status_string(status: int) -> str:
+    try:
+        return load().mfa_status_string(status).decode()
+    except Exception:  # the library itself may be what failed to load
+        return f"status {status}"
+
+
+def fwd(params: MfaFwdParams, stream: int) -> int:
+    return load().mfa_fwd(ctypes.byref(params), ctypes.c_void_p(stream))
+
+
+def select_kernel(params: MfaFwdParams) -> int:
+    return load().mfa_select_kernel(ctypes.byref(params))
+
+
+def lse_combine(o_ptrs, lse_ptrs, rows, H, D, o_ptr, o_dtype, lse_ptr, stream) -> int:
+    n = len(o_ptrs)
+    oa = (ctypes.c_void_p * n)(*o_ptrs)
+    la = (ctypes.c_void_p * n)(*lse_ptrs)
+    return load().mfa_lse_combine(oa, la, n, rows, H, D, ctypes.c_void_p(o_ptr), o_dtype,
+                                  ctypes.c_void_p(lse_ptr or 0), ctypes.c_void_p(stream))

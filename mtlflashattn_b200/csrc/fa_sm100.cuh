@@ -1,0 +1,409 @@
+// Flash-attention forward for B200 (sm_100a): TMA -> mbarrier ring -> tcgen05.mma with TMEM
+// accumulators -> fp32 online softmax in registers -> P back to TMEM -> P.V on tcgen05.
+//
+// One CTA owns 256 query rows of one (batch, head) as two 128-row tiles (t = 0, 1) and streams
+// the key/value blocks (128 keys each) that any of those rows may attend.
+//
+//   warps 0-3  softmax for tile 0   (TMEM lanes 0-127, one query row per thread)
+//   warps 4-7  softmax for tile 1
+//   warp  8    TMA producer: Q tiles once, then K_j, V_j into a shared ring of NSLOT slots
+//   warp  9    TMEM allocator + single-thread tcgen05.mma issuer
+//
+// TMEM columns (512 allocated): S0 [0,128) S1 [128,256) O0 [256,256+DP) O1 [256+DP,256+2DP).
+// P_t (16-bit, two per column) overwrites the first 64 columns of S_t once S_t is in registers.
+// The MMA warp issues, per key block j:  PV0_j, S0_{j+1}, PV1_j, S1_{j+1}.  tcgen05 MMAs of
+// one thread execute in issue order, so S_t(j+1) never overwrites P_t(j) before PV_t(j) read it,
+// and the commit that publishes S_t(j+1) also covers PV_t(j); that is what lets the softmax
+// warps rescale O_t in place right after they see S_t(j+1).
+//
+// Semantics follow the reference's chunked-fp32 tier (metal_flash_attn/_kernel.py:1165-1208):
+// scale, softcap, ALiBi, bottom-right causal and sliding window, fully masked rows -> 0.
+// The online softmax keeps a stale row maximum until it grows by more than 2^8 (log2 domain),
+// so O is rescaled rarely; the final 1/l uses the same maximum as O, so the result is exact.
+#pragma once
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace mfa {
+
+struct Sm100Args {
+  CUtensorMap tq, tk, tv;  // 4-D maps (D, H, S, B), box (64, 1, 128, 1), 128B swizzle
+  FwdArgs a;
+};
+
+namespace sm100 {
+
+constexpr int BM = 128;  // query rows per tile (TMEM lanes)
+constexpr int BN = 128;  // keys per block
+constexpr int kThreads = 320;
+
+template <int DP>
+struct Cfg {
+  static constexpr int NCH = DP / 64;                    // 128-byte column chunks per row
+  static constexpr uint32_t CHUNK = 128u * 128u;         // one chunk of 128 rows: 16 KB
+  static constexpr uint32_t TILE = NCH * CHUNK;          // Q tile or K / V block
+  static constexpr int NSLOT = DP == 128 ? 3 : 6;        // K/V ring depth
+  static constexpr uint32_t BAR_OFF = 2 * TILE + NSLOT * TILE;
+  static constexpr uint32_t SMEM = BAR_OFF + 256 + 1024;  // + barriers + alignment slack
+};
+
+// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.
+// K-major tiles (Q, K): SBO = 1024 B between 8-row groups; LBO unused (1).
+// MN-major tile (V as the B operand of P.V): LBO = 16 KB between 64-column chunks,
+// SBO = 1024 B between 8-key groups.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor for kind::f16: fp32 accumulator, A/B fp16 (0) or bf16 (1).
+__host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b_mn_major) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
+         ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+}  // namespace sm100
+
+template <int DP, bool kBF16, bool kGeneral>
+__global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_constant__ Sm100Args args) {
+  using namespace sm100;
+  using C = Cfg<DP>;
+  const FwdArgs& a = args.a;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* sb = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* sQ = sb;
+  uint8_t* sKV = sb + 2 * C::TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sb + C::BAR_OFF);
+  uint64_t* q_full = bars;                 // [2]
+  uint64_t* kv_full = bars + 2;            // [NSLOT]
+  uint64_t* kv_empty = kv_full + C::NSLOT; // [NSLOT]
+  uint64_t* s_full = kv_empty + C::NSLOT;  // [2]
+  uint64_t* p_full = s_full + 2;           // [2]
+  uint64_t* o_full = p_full + 2;           // [2]
+  uint64_t* mma_done = o_full + 2;         // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  // ---- work decode: heaviest row blocks first across all (batch, head)
+  const int HB = a.Hq * a.B;
+  const int idx = blockIdx.x;
+  const int rb = a.num_row_blocks - 1 - idx / HB;
+  const int hb = idx % HB;
+  const int h = hb % a.Hq;
+  const int b = hb / a.Hq;
+  const int hk = h / a.group;
+  const SeqView sv = seq_view(a, b);
+  const int r0 = rb * 2 * BM;
+  if (r0 >= sv.lq) return;  // whole CTA leaves before touching barriers or TMEM
+
+  const int r_last = min(r0 + 2 * BM, sv.lq) - 1;
+  const KeyRange kr_first = key_range(a, sv, r0);
+  const KeyRange kr_last = key_range(a, sv, r_last);
+  // union of the rows' intervals: lo is nondecreasing in the row, hi too
+  const int klo = kr_first.lo;
+  const int khi = kr_last.hi;
+  const int jb = klo / BN;
+  const int n = khi > klo ? (khi + BN - 1) / BN - jb : 0;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full[0], 1);
+    mbar_init(&q_full[1], 1);
+    for (int i = 0; i < C::NSLOT; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_full[t], 1);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_map(&args.tq);
+    tma_prefetch_map(&args.tk);
+    tma_prefetch_map(&args.tv);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    if (n > 0) {
+      const int qrow = sv.q0 + r0;
+      if (lane == 0) {
+        for (int t = 0; t < 2; ++t) {
+          mbar_expect_tx(&q_full[t], C::TILE);
+          for (int c = 0; c < C::NCH; ++c)
+            tma_load_4d(sQ + t * C::TILE + c * C::CHUNK, &args.tq, &q_full[t], 64 * c, h,
+                        qrow + t * BM, sv.qb);
+        }
+      }
+      for (int it = 0; it < 2 * n; ++it) {
+        const int slot = it % C::NSLOT;
+        const uint32_t ph = (uint32_t)(it / C::NSLOT) & 1u;
+        bool ok = mbar_wait(&kv_empty[slot], ph ^ 1u, abort_flag);
+        if (!__all_sync(kFull, ok)) break;
+        if (lane == 0) {
+          const int j = jb + (it >> 1);
+          const CUtensorMap* m = (it & 1) ? &args.tv : &args.tk;
+          mbar_expect_tx(&kv_full[slot], C::TILE);
+          for (int c = 0; c < C::NCH; ++c)
+            tma_load_4d(sKV + slot * C::TILE + c * C::CHUNK, m, &kv_full[slot], 64 * c, hk,
+                        sv.k0 + j * BN, sv.kb);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t kIdQK = idesc_f16(kBF16, BM, BN, false);
+    constexpr uint32_t kIdPV = idesc_f16(kBF16, BM, DP, true);
+    const uint32_t sQa = smem_u32(sQ);
+    const uint32_t sKVa = smem_u32(sKV);
+    bool ok = true;
+    auto qk = [&](int t, int slot) {  // S_t = Q_t K^T
+#pragma unroll
+      for (int k = 0; k < DP / 16; ++k) {
+        const uint32_t koff = (k >> 2) * C::CHUNK + (k & 3) * 32;
+        mma_ss(tmem + 128u * t, desc_sw128(sQa + t * C::TILE + koff, 16, 1024),
+               desc_sw128(sKVa + slot * C::TILE + koff, 16, 1024), kIdQK, k > 0);
+      }
+    };
+    auto pv = [&](int t, int slot, bool acc) {  // O_t (+)= P_t V
+#pragma unroll
+      for (int k = 0; k < BN / 16; ++k)
+        mma_ts(tmem + 256u + DP * t, tmem + 128u * t + k * 8, desc_sw128(sKVa + slot * C::TILE + k * 2048, C::CHUNK, 1024),
+               kIdPV, (acc || k > 0) ? 1u : 0u);
+    };
+    if (n > 0) {
+      ok = mbar_wait(&q_full[0], 0, abort_flag) && mbar_wait(&q_full[1], 0, abort_flag);
+      ok = __all_sync(kFull, ok);
+      int slotK = 0;
+      if (ok) {
+        ok = __all_sync(kFull, mbar_wait(&kv_full[0], 0, abort_flag));
+      }
+      if (ok) {
+        tc_fence_after();
+        if (lane == 0) {
+          qk(0, 0);
+          tc_commit(&s_full[0]);
+          qk(1, 0);
+          tc_commit(&s_full[1]);
+          tc_commit(&kv_empty[0]);
+        }
+        __syncwarp();
+      }
+      for (int j = 0; j < n && ok; ++j) {
+        const int itV = 2 * j + 1;
+        const int slotV = itV % C::NSLOT;
+        ok = mbar_wait(&kv_full[slotV], (uint32_t)(itV / C::NSLOT) & 1u, abort_flag);
+        ok = __all_sync(kFull, ok && mbar_wait(&p_full[0], (uint32_t)j & 1u, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
+          pv(0, slotV, j > 0);
+          if (j == n - 1) tc_commit(&o_full[0]);
+        }
+        __syncwarp();
+        const bool more = j + 1 < n;
+        if (more) {
+          const int itK = 2 * j + 2;
+          slotK = itK % C::NSLOT;
+          ok = __all_sync(kFull, mbar_wait(&kv_full[slotK], (uint32_t)(itK / C::NSLOT) & 1u, abort_flag));
+          if (!ok) break;
+          tc_fence_after();
+          if (lane == 0) {
+            qk(0, slotK);
+            tc_commit(&s_full[0]);
+          }
+          __syncwarp();
+        }
+        ok = __all_sync(kFull, mbar_wait(&p_full[1], (uint32_t)j & 1u, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
+          pv(1, slotV, j > 0);
+          tc_commit(&kv_empty[slotV]);
+          if (j == n - 1) tc_commit(&o_full[1]);
+          if (more) {
+            qk(1, slotK);
+            tc_commit(&s_full[1]);
+            tc_commit(&kv_empty[slotK]);
+          }
+        }
+        __syncwarp();
+      }
+      // Drain: every MMA issued above has completed before TMEM is released.
+      if (lane == 0) tc_commit(mma_done);
+      __syncwarp();
+      if (!mbar_wait_drain(mma_done, 0)) *abort_flag = 1;
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warpgroups
+    const int t = warp >> 2;        // tile
+    const int wq = warp & 3;        // TMEM lane quarter
+    const int rt = wq * 32 + lane;  // row within tile
+    const int64_t row = (int64_t)r0 + t * BM + rt;  // row within the sequence
+    const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+    const uint32_t tS = tmem + lane_base + t * 128;
+    const uint32_t tO = tmem + lane_base + 256 + t * DP;
+    const KeyRange kr = key_range(a, sv, row);
+    // tile-uniform interval extremes for the "block needs no mask" test
+    const int tile_lo_max = key_range(a, sv, (int64_t)r0 + t * BM + BM - 1).lo;
+    const int tile_hi_min = key_range(a, sv, (int64_t)r0 + t * BM).hi;
+    constexpr float kLog2e = 1.4426950408889634f;
+    const float c = kGeneral ? 1.f : a.scale * kLog2e;  // multiplies x to reach log2 units
+    float slope = 0.f;
+    if (kGeneral && a.alibi != nullptr) slope = a.alibi[(int64_t)b * a.Hq + h];
+    const float centre = (float)(row + sv.off);
+    const float cap = a.softcap;
+
+    float m_used = -INFINITY;  // in x units
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      ok = __all_sync(kFull, mbar_wait(&s_full[t], (uint32_t)j & 1u, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t r[128];
+      tmem_ld32(tS + 0, r);
+      tmem_ld32(tS + 32, r + 32);
+      tmem_ld32(tS + 64, r + 64);
+      tmem_ld32(tS + 96, r + 96);
+      tmem_ld_wait32(r);
+      tmem_ld_tie32(r + 32);
+      tmem_ld_tie32(r + 64);
+      tmem_ld_tie32(r + 96);
+      float x[128];
+      const int c0 = (jb + j) * BN;
+      const bool need_mask = (c0 < tile_lo_max) || (c0 + BN > tile_hi_min);
+      if constexpr (kGeneral) {
+        // x = log2(e) * (softcap(s * scale) - slope * |centre - key|), masked -> -inf
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          float s = __uint_as_float(r[i]) * a.scale;
+          if (cap > 0.f) s = cap * tanh_exp2(s / cap);
+          const int kl = c0 + i;
+          s -= slope * fabsf(centre - (float)(kl + a.k_pos_offset));
+          x[i] = s * kLog2e;
+          if (need_mask && (kl < kr.lo || kl >= kr.hi)) x[i] = -INFINITY;
+        }
+      } else {
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i) {
+            const int kl = c0 + i;
+            x[i] = (kl < kr.lo || kl >= kr.hi) ? -INFINITY : __uint_as_float(r[i]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 128; ++i) x[i] = __uint_as_float(r[i]);
+        }
+      }
+      float mx0 = x[0], mx1 = x[1], mx2 = x[2], mx3 = x[3];
+#pragma unroll
+      for (int i = 4; i < 128; i += 4) {
+        mx0 = fmaxf(mx0, x[i]);
+        mx1 = fmaxf(mx1, x[i + 1]);
+        mx2 = fmaxf(mx2, x[i + 2]);
+        mx3 = fmaxf(mx3, x[i + 3]);
+      }
+      const float m_new = fmaxf(m_used, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)));
+      const bool grow = (m_new - m_used) * c > 8.f;  // false when both are -inf (NaN compare)
+      if (__any_sync(kFull, grow)) {
+        const float factor = (m_used == -INFINITY) ? 0.f : ex2((m_used - m_new) * c);
+        if (j > 0) {
+          // O_t is idle here: the commit that published S_t(j) also covered PV_t(j-1).
+#pragma unroll 1
+          for (int cc = 0; cc < DP; cc += 32) {
+            uint32_t o[32];
+            tmem_ld32(tO + cc, o);
+            tmem_ld_wait32(o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+            tmem_st32(tO + cc, o);
+          }
+        }
+        l *= factor;
+        m_used = m_new;
+      }
+      const float ref = (m_used == -INFINITY) ? 0.f : m_used * c;
+      float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {  // 32 keys -> 16 packed columns per store
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = ex2(fmaf(x[32 * cc + 2 * i], c, -ref));
+          const float p1 = ex2(fmaf(x[32 * cc + 2 * i + 1], c, -ref));
+          l0 += p0;
+          l1 += p1;
+          pk[i] = pack2<kBF16>(p0, p1);
+        }
+        tmem_st16(tS + 16 * cc, pk);
+      }
+      l += l0 + l1;
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if (ok && n > 0) ok = __all_sync(kFull, mbar_wait(&o_full[t], 0, abort_flag));
+    if (ok) {
+      tc_fence_after();
+      const bool store = row < sv.lq;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint8_t* orow = nullptr;
+      if (store) {
+        const int64_t esz = a.o_dtype == 2 ? 4 : 2;
+        orow = reinterpret_cast<uint8_t*>(a.o) +
+               esz * ((int64_t)sv.qb * a.o_sb + (int64_t)(sv.q0 + row) * a.o_ss + (int64_t)h * a.o_sh);
+      }
+#pragma unroll 1
+      for (int cc = 0; cc < DP; cc += 32) {
+        float vals[32];
+        if (n > 0) {
+          uint32_t o[32];
+          tmem_ld32(tO + cc, o);
+          tmem_ld_wait32(o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) vals[i] = __uint_as_float(o[i]) * inv;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) vals[i] = 0.f;
+        }
+        const int nc = min(32, a.D - cc);
+        if (store && nc > 0) store_row_chunk(a, orow, cc, vals, nc);
+      }
+      if (store && a.lse != nullptr) {
+        const float lse = l > 0.f ? (m_used * c + __log2f(l)) * 0.6931471805599453f : -INFINITY;
+        a.lse[(int64_t)sv.qb * a.lse_sb + (int64_t)h * a.lse_sh + sv.q0 + row] = lse;
+      }
+    }
+  }
+
+  // ---- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+  if (threadIdx.x == 0 && *abort_flag && a.err != nullptr) atomicExch(a.err, 4 /*MFA_ERR_TIMEOUT*/);
+}
+
+}  // namespace mfa

@@ -1,0 +1,343 @@
+// C ABI of libmfa.so (declared in include/mfa.h): argument checks, kernel choice, TMA tensor
+// maps and launches. Replaces the tier dispatch of the reference's flash_attn_forward
+// (metal_flash_attn/_kernel.py:1052-1153) and its Metal launchers (_kernel.py:1288-1420).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/mfa.h"
+#include "fa_simt.cuh"
+#include "fa_sm100.cuh"
+
+namespace mfa {
+namespace {
+
+// ------------------------------------------------------------------ host fault injection
+// MFA_FAULT=<site>[,<site>...] makes the named entry point fail before it launches anything,
+// so callers' error handling can be tested without touching a GPU. Sites: fwd, combine.
+bool fault_injected(const char* site) {
+  const char* env = std::getenv("MFA_FAULT");
+  if (env == nullptr || *env == 0) return false;
+  const size_t n = std::strlen(site);
+  for (const char* p = env; *p;) {
+    const char* e = std::strchr(p, ',');
+    const size_t len = e ? (size_t)(e - p) : std::strlen(p);
+    if (len == n && std::strncmp(p, site, n) == 0) return true;
+    if (!e) break;
+    p = e + 1;
+  }
+  return false;
+}
+
+// ------------------------------------------------------------------ driver entry point
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+struct DevInfo {
+  int major = -1, minor = -1, sms = 0;
+};
+DevInfo dev_info(int dev) {
+  static std::mutex mu;
+  static DevInfo cache[64];
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev < 0 || dev >= 64) return DevInfo{};
+  if (cache[dev].major < 0) {
+    cudaDeviceGetAttribute(&cache[dev].major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&cache[dev].minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&cache[dev].sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return cache[dev];
+}
+
+// cudaFuncSetAttribute once per (kernel, device).
+template <typename K>
+cudaError_t ensure_smem(K kernel, int dev, int bytes) {
+  static std::mutex mu;
+  static const void* seen[256];
+  static int seen_dev[256];
+  static int nseen = 0;
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < nseen; ++i)
+    if (seen[i] == (const void*)kernel && seen_dev[i] == dev) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && nseen < 256) {
+    seen[nseen] = (const void*)kernel;
+    seen_dev[nseen] = dev;
+    ++nseen;
+  }
+  return e;
+}
+
+int esize(int dtype) { return dtype == MFA_FP32 ? 4 : 2; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Argument checks. Mirrors the checks the reference makes before any tier runs
+// (metal_flash_attn/__init__.py:28-59, 84-90; _kernel.py:1070-1074, 1145-1147).
+int validate(const mfa_fwd_params* p) {
+  if (p == nullptr) return MFA_ERR_INVALID;
+  if (p->dtype < 0 || p->dtype > 2) return MFA_ERR_UNSUPPORTED;
+  const int od = p->o_dtype < 0 ? p->dtype : p->o_dtype;
+  if (od > 2) return MFA_ERR_UNSUPPORTED;
+  if (p->D < 1 || p->D > 128) return MFA_ERR_UNSUPPORTED;
+  if (p->B < 0 || p->Hq < 1 || p->Hkv < 1 || p->Hq % p->Hkv != 0) return MFA_ERR_INVALID;
+  if (!(p->softcap >= 0.f)) return MFA_ERR_INVALID;
+  if (p->win_left < -1 || p->win_right < -1) return MFA_ERR_INVALID;
+  const bool varlen = p->cu_q != nullptr || p->cu_k != nullptr;
+  if (varlen && (p->cu_q == nullptr || p->cu_k == nullptr)) return MFA_ERR_INVALID;
+  if (!varlen && (p->Lq < 0 || p->Lk < 0)) return MFA_ERR_INVALID;
+  if (varlen && p->max_lq < 0) return MFA_ERR_INVALID;
+  if (p->B == 0 || (!varlen && p->Lq == 0) || (varlen && p->max_lq == 0)) return MFA_OK;
+  if (p->q == nullptr || p->k == nullptr || p->v == nullptr || p->o == nullptr)
+    return MFA_ERR_INVALID;
+  return MFA_OK;
+}
+
+FwdArgs resolve(const mfa_fwd_params* p) {
+  FwdArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.q = p->q;
+  a.k = p->k;
+  a.v = p->v;
+  a.o = p->o;
+  a.lse = p->lse;
+  a.q_sb = p->q_stride[0]; a.q_ss = p->q_stride[1]; a.q_sh = p->q_stride[2];
+  a.k_sb = p->k_stride[0]; a.k_ss = p->k_stride[1]; a.k_sh = p->k_stride[2];
+  a.v_sb = p->v_stride[0]; a.v_ss = p->v_stride[1]; a.v_sh = p->v_stride[2];
+  a.o_sb = p->o_stride[0]; a.o_ss = p->o_stride[1]; a.o_sh = p->o_stride[2];
+  a.lse_sb = p->lse_stride[0];
+  a.lse_sh = p->lse_stride[1];
+  a.B = p->B;
+  a.Hq = p->Hq;
+  a.Hkv = p->Hkv;
+  a.Lq = p->Lq;
+  a.Lk = p->Lk;
+  a.D = p->D;
+  a.group = p->Hq / p->Hkv;
+  a.cu_q = p->cu_q;
+  a.cu_k = p->cu_k;
+  a.max_lq = p->cu_q ? p->max_lq : p->Lq;
+  a.scale = p->scale;
+  a.softcap = p->softcap;
+  a.causal = p->causal ? 1 : 0;
+  a.wl = p->win_left;
+  a.wr = p->win_right;
+  a.alibi = p->alibi;
+  a.o_dtype = p->o_dtype < 0 ? p->dtype : p->o_dtype;
+  const int oes = esize(a.o_dtype);
+  a.o_vec16 = aligned16(p->o) && (a.o_ss * oes) % 16 == 0 && (a.o_sh * oes) % 16 == 0 &&
+              (p->cu_q != nullptr || (a.o_sb * oes) % 16 == 0);
+  a.k_pos_offset = p->k_pos_offset;
+  a.lk_total = p->lk_total;
+  a.err = p->err;
+  return a;
+}
+
+// tcgen05 path eligibility: 16-bit inputs, D a multiple of 8 (TMA needs 16-byte strides),
+// 16-byte aligned bases and strides, and an sm_100 device.
+bool tc_eligible(const mfa_fwd_params* p, const DevInfo& di) {
+  if (di.major != 10 || di.minor != 0) return false;
+  if (p->dtype != MFA_FP16 && p->dtype != MFA_BF16) return false;
+  if (p->D % 8 != 0) return false;
+  const void* ptrs[3] = {p->q, p->k, p->v};
+  const int64_t* strides[3] = {p->q_stride, p->k_stride, p->v_stride};
+  const bool varlen = p->cu_q != nullptr;
+  for (int i = 0; i < 3; ++i) {
+    if (!aligned16(ptrs[i])) return false;
+    const int64_t extent[3] = {varlen ? 1 : p->B, i == 0 ? p->Lq : p->Lk, i == 0 ? p->Hq : p->Hkv};
+    for (int d = 0; d < 3; ++d) {
+      if (extent[d] <= 1) continue;  // a unit dimension's stride is never used
+      const int64_t s = strides[i][d] * 2;
+      if (s <= 0 || s % 16 != 0 || s >= (1ll << 40)) return false;
+    }
+  }
+  return true;
+}
+
+int pick_kernel(const mfa_fwd_params* p, int dev) {
+  const DevInfo di = dev_info(dev);
+  if (p->kernel == MFA_KERNEL_SIMT) return MFA_KERNEL_SIMT;
+  // An empty key set has nothing to stream; the CUDA-core kernel writes the zero rows.
+  const bool ok = tc_eligible(p, di) && p->Lk > 0;
+  if (p->kernel == MFA_KERNEL_TCGEN05) return ok ? MFA_KERNEL_TCGEN05 : -MFA_ERR_UNSUPPORTED;
+  return ok ? MFA_KERNEL_TCGEN05 : MFA_KERNEL_SIMT;
+}
+
+// 4-D tensor map over (D, H, S, B) with a (64, 1, 128, 1) box and 128-byte swizzle.
+int make_map(CUtensorMap* m, const void* base, int dtype, int D, int H, int64_t S, int B,
+             const int64_t* stride /* batch, seq, head (elements) */) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return MFA_ERR_CUDA;
+  const int64_t es = 2;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)(S > 0 ? S : 1),
+                        (cuuint64_t)(B > 0 ? B : 1)};
+  int64_t sh = stride[2] * es, ss = stride[1] * es, sbt = stride[0] * es;
+  // a unit dimension's stride is never used, but must be encodable
+  if (H <= 1) sh = 16;
+  if (S <= 1) ss = 16;
+  if (B <= 1) sbt = 16;
+  cuuint64_t strides[3] = {(cuuint64_t)sh, (cuuint64_t)ss, (cuuint64_t)sbt};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, dtype == MFA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                  4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MFA_OK : MFA_ERR_CUDA;
+}
+
+template <int DP, bool BF16, bool GEN>
+int launch_sm100(const Sm100Args& args, int dev, int64_t grid, cudaStream_t st) {
+  auto k = fa_fwd_sm100<DP, BF16, GEN>;
+  const int smem = (int)sm100::Cfg<DP>::SMEM;
+  if (ensure_smem(k, dev, smem) != cudaSuccess) return MFA_ERR_CUDA;
+  k<<<(unsigned)grid, sm100::kThreads, smem, st>>>(args);
+  return MFA_OK;
+}
+
+int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st) {
+  Sm100Args args;
+  std::memset(&args, 0, sizeof(args));
+  const bool varlen = p->cu_q != nullptr;
+  const int64_t Sq = varlen ? p->Lq : p->Lq;  // varlen: Lq carries total_q
+  const int64_t Sk = varlen ? p->Lk : p->Lk;
+  const int Bm = varlen ? 1 : p->B;
+  int rc;
+  if ((rc = make_map(&args.tq, p->q, p->dtype, p->D, p->Hq, Sq, Bm, p->q_stride)) != MFA_OK) return rc;
+  if ((rc = make_map(&args.tk, p->k, p->dtype, p->D, p->Hkv, Sk, Bm, p->k_stride)) != MFA_OK) return rc;
+  if ((rc = make_map(&args.tv, p->v, p->dtype, p->D, p->Hkv, Sk, Bm, p->v_stride)) != MFA_OK) return rc;
+  a.num_row_blocks = (a.max_lq + 2 * sm100::BM - 1) / (2 * sm100::BM);
+  args.a = a;
+  const int64_t grid = (int64_t)a.num_row_blocks * a.Hq * a.B;
+  if (grid == 0) return MFA_OK;
+  if (grid >= (1ll << 31)) return MFA_ERR_UNSUPPORTED;
+  const bool gen = !(a.scale > 0.f) || a.softcap > 0.f || a.alibi != nullptr;
+  const bool bf = p->dtype == MFA_BF16;
+  const bool wide = p->D > 64;
+#define MFA_SM100(DP, BF, G) return launch_sm100<DP, BF, G>(args, dev, grid, st)
+  if (wide) {
+    if (bf) { if (gen) MFA_SM100(128, true, true); MFA_SM100(128, true, false); }
+    if (gen) MFA_SM100(128, false, true);
+    MFA_SM100(128, false, false);
+  }
+  if (bf) { if (gen) MFA_SM100(64, true, true); MFA_SM100(64, true, false); }
+  if (gen) MFA_SM100(64, false, true);
+  MFA_SM100(64, false, false);
+#undef MFA_SM100
+}
+
+template <typename T, int DP>
+int launch_simt(const FwdArgs& a, int64_t grid, cudaStream_t st) {
+  fa_fwd_simt<T, DP><<<(unsigned)grid, simt::kThreads, 0, st>>>(a);
+  return MFA_OK;
+}
+
+int run_simt(const mfa_fwd_params* p, FwdArgs a, cudaStream_t st) {
+  a.num_row_blocks = (a.max_lq + simt::BM - 1) / simt::BM;
+  const int64_t grid = (int64_t)a.num_row_blocks * a.Hq * a.B;
+  if (grid == 0) return MFA_OK;
+  if (grid >= (1ll << 31)) return MFA_ERR_UNSUPPORTED;
+  const int dp = p->D <= 32 ? 32 : (p->D <= 64 ? 64 : 128);
+#define MFA_SIMT(T)                                        \
+  do {                                                     \
+    if (dp == 32) return launch_simt<T, 32>(a, grid, st);  \
+    if (dp == 64) return launch_simt<T, 64>(a, grid, st);  \
+    return launch_simt<T, 128>(a, grid, st);               \
+  } while (0)
+  if (p->dtype == MFA_FP32) MFA_SIMT(float);
+  if (p->dtype == MFA_BF16) MFA_SIMT(__nv_bfloat16);
+  MFA_SIMT(__half);
+#undef MFA_SIMT
+}
+
+}  // namespace
+}  // namespace mfa
+
+extern "C" {
+
+int mfa_abi_version(void) { return MFA_ABI_VERSION; }
+
+const char* mfa_status_string(int s) {
+  switch (s) {
+    case MFA_OK: return "ok";
+    case MFA_ERR_INVALID: return "invalid argument";
+    case MFA_ERR_UNSUPPORTED: return "unsupported shape, dtype or kernel for this input";
+    case MFA_ERR_CUDA: return "CUDA error";
+    case MFA_ERR_TIMEOUT: return "in-kernel wait timed out";
+    case MFA_ERR_NO_DEVICE: return "no usable CUDA device";
+    case MFA_ERR_FAULT_INJECTED: return "fault injected (MFA_FAULT)";
+    default: return "unknown status";
+  }
+}
+
+int mfa_select_kernel(const mfa_fwd_params* p) {
+  int rc = mfa::validate(p);
+  if (rc != MFA_OK) return -rc;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -MFA_ERR_NO_DEVICE;
+  return mfa::pick_kernel(p, dev);
+}
+
+int mfa_fwd(const mfa_fwd_params* p, void* stream) {
+  if (mfa::fault_injected("fwd")) return MFA_ERR_FAULT_INJECTED;
+  int rc = mfa::validate(p);
+  if (rc != MFA_OK) return rc;
+  const bool varlen = p->cu_q != nullptr;
+  if (p->B == 0 || (!varlen && p->Lq == 0) || (varlen && p->max_lq == 0)) return MFA_OK;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MFA_ERR_NO_DEVICE;
+  const int kern = mfa::pick_kernel(p, dev);
+  if (kern < 0) return -kern;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  (void)cudaGetLastError();
+  mfa::FwdArgs a = mfa::resolve(p);
+  rc = kern == MFA_KERNEL_TCGEN05 ? mfa::run_sm100(p, a, dev, st) : mfa::run_simt(p, a, st);
+  if (rc != MFA_OK) return rc;
+  return cudaGetLastError() == cudaSuccess ? MFA_OK : MFA_ERR_CUDA;
+}
+
+int mfa_lse_combine(const float* const* o_part, const float* const* lse_part, int32_t n,
+                    int32_t rows, int32_t H, int32_t D, void* o, int32_t o_dtype, float* lse,
+                    void* stream) {
+  if (mfa::fault_injected("combine")) return MFA_ERR_FAULT_INJECTED;
+  if (n < 1 || n > mfa::kMaxParts || rows < 0 || H < 1 || D < 1 || o_dtype < 0 || o_dtype > 2)
+    return MFA_ERR_INVALID;
+  if (rows == 0) return MFA_OK;
+  if (o_part == nullptr || lse_part == nullptr || o == nullptr) return MFA_ERR_INVALID;
+  mfa::PartPtrs pp;
+  std::memset(&pp, 0, sizeof(pp));
+  for (int g = 0; g < n; ++g) {
+    if (o_part[g] == nullptr || lse_part[g] == nullptr) return MFA_ERR_INVALID;
+    pp.o[g] = o_part[g];
+    pp.lse[g] = lse_part[g];
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  (void)cudaGetLastError();
+  const int64_t warps = (int64_t)rows * H;
+  const unsigned blocks = (unsigned)((warps * 32 + 255) / 256);
+  if (o_dtype == MFA_FP32)
+    mfa::lse_combine_kernel<float><<<blocks, 256, 0, st>>>(pp, n, rows, H, D, (float*)o, lse);
+  else if (o_dtype == MFA_BF16)
+    mfa::lse_combine_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(pp, n, rows, H, D, (__nv_bfloat16*)o, lse);
+  else
+    mfa::lse_combine_kernel<__half><<<blocks, 256, 0, st>>>(pp, n, rows, H, D, (__half*)o, lse);
+  return cudaGetLastError() == cudaSuccess ? MFA_OK : MFA_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -1,0 +1,270 @@
+"""Parity of the CUDA paths (tcgen05 and SIMT kernels, through the public API and the C ABI)
+with the reference: the golden outputs the reference itself produced, and the oracle
+(a restatement of the reference's chunked-fp32 tier) on the same seeded inputs.
+
+Tolerances are the reference's own (tests/test_flash_attn_func.py:62-66): fp32 atol 2e-5
+rtol 1e-4; fp16 atol 1.5e-2 rtol 2e-2; bf16 atol 2e-2 rtol 2e-2. The BASELINE configurations
+are held to the engine's stated bar: max abs error <= 1e-2 for fp16/bf16 outputs against the
+fp32 oracle, <= 5e-4 for fp32.
+"""
+import math
+import os
+
+import pytest
+import torch
+
+import mtlflashattn_b200 as mfa
+from golden.cases import load_cases
+from oracle import flash_torch as ref
+
+pytestmark = pytest.mark.gpu
+
+TOL = {
+    torch.float32: dict(atol=2e-5, rtol=1e-4),
+    torch.float16: dict(atol=1.5e-2, rtol=2e-2),
+    torch.bfloat16: dict(atol=2e-2, rtol=2e-2),
+}
+BAR = {torch.float32: 5e-4, torch.float16: 1e-2, torch.bfloat16: 1e-2}
+DEV = "cuda"
+CASES = load_cases()
+
+
+@pytest.fixture(autouse=True)
+def _sync_check(monkeypatch):
+    monkeypatch.setenv("MTLFLASHATTN_SYNC_CHECK", "1")
+    yield
+
+
+def run_case(case, device=DEV):
+    q, k, v = (t.to(device) for t in (case["q"], case["k"], case["v"]))
+    alibi = case["alibi"].to(device) if case["alibi"] is not None else None
+    kw = dict(softmax_scale=case["scale"], causal=case["causal"], window_size=case["window"],
+              softcap=case["softcap"], alibi_slopes=alibi)
+    if case["kind"] == "dense":
+        return mfa.flash_attn_func(q, k, v, **kw)
+    lq, lk = case["lq"], case["lk"]
+    return mfa.flash_attn_varlen_func(q, k, v, case["cu_q"].to(device), case["cu_k"].to(device),
+                                      max(lq), max(lk), **kw)
+
+
+def check_close(out, want, dtype, what=""):
+    err = (out.float().cpu() - want.float().cpu()).abs().max().item() if out.numel() else 0.0
+    assert out.dtype == dtype
+    torch.testing.assert_close(out.float().cpu(), want.float().cpu(), **TOL[dtype],
+                               msg=lambda m: f"{what}: max abs err {err:.3e}\n{m}")
+    return err
+
+
+def tc_eligible(case):
+    d = case["D"] if case["kind"] == "varlen" else case["shape"][5]
+    return case["dtype"] != torch.float32 and d % 8 == 0
+
+
+@pytest.mark.parametrize("kernel", ["auto", "simt", "tcgen05"])
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_golden(case, kernel, monkeypatch):
+    if kernel == "tcgen05" and not tc_eligible(case):
+        pytest.skip("tcgen05 needs fp16/bf16 and D % 8 == 0")
+    monkeypatch.setenv("MTLFLASHATTN_KERNEL", kernel)
+    out = run_case(case)
+    want = case["out_f32"] if case["out_f32"] is not None else case["out"]
+    check_close(out, want, case["dtype"], f"{case['name']}[{kernel}]")
+
+
+def _cfg_inputs(cfg):
+    if cfg == 2:
+        q, k, v = ref.make_qkv(1, 8192, 8192, 16, 16, 64, torch.bfloat16, seed=0)
+        return (q, k, v), dict(causal=True)
+    if cfg == 3:
+        q, k, v = ref.make_qkv(1, 8192, 8192, 16, 16, 128, torch.float16, seed=0)
+        return (q, k, v), dict(softcap=30.0, window_size=(1024, 1024))
+    if cfg == "target":
+        q, k, v = ref.make_qkv(1, 8192, 8192, 16, 16, 128, torch.bfloat16, seed=0)
+        return (q, k, v), dict(causal=True)
+    raise ValueError(cfg)
+
+
+@pytest.mark.parametrize("cfg", [2, 3, "target"])
+def test_baseline_config_dense(cfg):
+    """Full-size BASELINE configs against the oracle run on the GPU in fp32 (same code as the
+    CPU oracle, on CUDA tensors so the 8k x 8k problems finish in seconds)."""
+    (q, k, v), kw = _cfg_inputs(cfg)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    out = mfa.flash_attn_func(qd, kd, vd, **kw)
+    want = ref.flash_attn_func(qd.float(), kd.float(), vd.float(), chunk=1024, **kw)
+    err = (out.float() - want).abs().max().item()
+    assert err <= BAR[q.dtype], f"config {cfg}: max abs err {err:.3e}"
+    # against the reference's own q.dtype output: the same fp32 result rounded once
+    err_cast = (out.float() - want.to(q.dtype).float()).abs().max().item()
+    assert err_cast <= 2 * BAR[q.dtype], f"config {cfg}: max abs err vs cast oracle {err_cast:.3e}"
+
+
+def test_baseline_config4_varlen_gqa_alibi():
+    lens = torch.randint(256, 8193, (16,), generator=torch.Generator().manual_seed(0)).tolist()
+    q, k, v, cu_q, cu_k = ref.make_varlen(lens, lens, 32, 8, 128, torch.bfloat16, seed=1)
+    slopes = torch.tensor([2 ** (-8 * (i + 1) / 32) for i in range(32)])
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    out = mfa.flash_attn_varlen_func(qd, kd, vd, cu_q.to(DEV), cu_k.to(DEV), max(lens), max(lens),
+                                     causal=True, alibi_slopes=slopes.to(DEV))
+    want = ref.flash_attn_varlen_func(qd.float(), kd.float(), vd.float(), cu_q, cu_k, causal=True,
+                                      alibi_slopes=slopes.to(DEV), chunk=1024)
+    err = (out.float() - want).abs().max().item()
+    assert err <= BAR[torch.bfloat16], f"config 4: max abs err {err:.3e}"
+
+
+def test_baseline_config5_suffix_rows():
+    """Config 5 (L=131072) checked on exact query-row suffixes: bottom-right alignment makes the
+    last r rows of the full problem equal a problem with Lq = r over the same keys."""
+    q, k, v = ref.make_qkv(1, 131072, 131072, 16, 16, 128, torch.float32, seed=0, scale_inputs=0.5)
+    q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    out = mfa.flash_attn_func(qd, kd, vd, causal=True)
+    r = 512
+    heads = [0, 7, 15]
+    want = ref.flash_attn_func(qd[:, -r:, heads].float(), kd[:, :, heads].float(),
+                               vd[:, :, heads].float(), causal=True, chunk=128)
+    err = (out[:, -r:, heads].float() - want).abs().max().item()
+    assert err <= 1e-2, f"config 5 suffix: max abs err {err:.3e}"
+    # the first rows too (a prefix of rows attends a prefix of keys under causal masking)
+    wantp = ref.flash_attn_func(qd[:, :r, heads].float(), kd[:, :r, heads].float(),
+                                vd[:, :r, heads].float(), causal=True)
+    errp = (out[:, :r, heads].float() - wantp).abs().max().item()
+    assert errp <= 1e-2, f"config 5 prefix: max abs err {errp:.3e}"
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("shape", [
+    (1, 1, 1, 1, 1, 64), (2, 257, 255, 4, 2, 128), (1, 129, 1000, 3, 1, 64),
+    (3, 300, 100, 2, 2, 96), (1, 513, 513, 2, 2, 40), (1, 256, 384, 2, 1, 8),
+])
+@pytest.mark.parametrize("causal", [False, True])
+def test_kernels_agree_random_shapes(shape, dtype, causal):
+    B, Lq, Lk, Hq, Hkv, D = shape
+    q, k, v = ref.make_qkv(B, Lq, Lk, Hq, Hkv, D, dtype, seed=Lq + Lk + D)
+    want = ref.flash_attn_func(q, k, v, causal=causal)
+    for kern in ("tcgen05", "simt"):
+        os.environ["MTLFLASHATTN_KERNEL"] = kern
+        try:
+            out = mfa.flash_attn_func(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+        finally:
+            del os.environ["MTLFLASHATTN_KERNEL"]
+        check_close(out, want, dtype, f"{shape} {kern}")
+
+
+def test_empty_and_degenerate_shapes():
+    for (B, Lq, Lk) in ((0, 16, 16), (1, 0, 16), (1, 16, 0)):
+        q, k, v = ref.make_qkv(max(B, 1), Lq, Lk, 2, 2, 64, torch.bfloat16)
+        q, k, v = q[:B], k[:B], v[:B]
+        out = mfa.flash_attn_func(q.to(DEV), k.to(DEV), v.to(DEV), causal=True)
+        assert out.shape == q.shape
+        if out.numel():
+            assert torch.count_nonzero(out) == 0  # no keys -> rows are 0 (nan_to_num)
+
+
+def test_fully_masked_rows_are_zero():
+    # causal with Lq > Lk: the first Lq - Lk rows have no key (reference test :100-102)
+    q, k, v = ref.make_qkv(1, 300, 100, 2, 2, 64, torch.bfloat16, seed=3)
+    out = mfa.flash_attn_func(q.to(DEV), k.to(DEV), v.to(DEV), causal=True)
+    assert torch.count_nonzero(out[:, :200]) == 0
+    check_close(out, ref.flash_attn_func(q, k, v, causal=True), torch.bfloat16)
+
+
+def test_strided_views_no_copy_semantics():
+    g = torch.Generator().manual_seed(0)
+    qkv = torch.randn(2, 300, 3, 4, 64, generator=g).to(DEV, torch.float16)
+    out_p = mfa.flash_attn_qkvpacked_func(qkv, causal=True)
+    q, k, v = qkv.unbind(dim=2)
+    out_u = mfa.flash_attn_func(q.contiguous(), k.contiguous(), v.contiguous(), causal=True)
+    torch.testing.assert_close(out_p, out_u, atol=0, rtol=0)
+
+
+def test_heads_second_boundary():
+    """flash_attn_forward keeps the reference boundary's contract: heads-second in, contiguous
+    [B, Hq, Lq, D] in q.dtype out."""
+    q, k, v = ref.make_qkv(2, 200, 230, 4, 2, 64, torch.bfloat16, seed=8)
+    qh, kh, vh = (t.to(DEV).transpose(1, 2) for t in (q, k, v))
+    out = mfa.flash_attn_forward(qh, kh, vh, scale=0.1, causal=True, softcap=10.0,
+                                 window_left=50, window_right=3,
+                                 alibi_slopes=torch.tensor([0.1, 0.2, 0.3, 0.4], device=DEV))
+    assert out.is_contiguous() and out.shape == (2, 4, 200, 64) and out.dtype == torch.bfloat16
+    want = ref.attention_heads_second(qh.cpu(), kh.cpu(), vh.cpu(), 0.1, True, 10.0, 50, 3,
+                                      torch.tensor([0.1, 0.2, 0.3, 0.4] * 2))
+    check_close(out, want, torch.bfloat16)
+
+
+def test_fp32_meets_reference_tolerance_long():
+    q, k, v = ref.make_qkv(1, 1500, 1700, 4, 2, 128, torch.float32, seed=2)
+    out = mfa.flash_attn_func(q.to(DEV), k.to(DEV), v.to(DEV), causal=True, softcap=20.0)
+    check_close(out, ref.flash_attn_func(q, k, v, causal=True, softcap=20.0), torch.float32)
+
+
+def test_varlen_single_sequence_matches_dense():
+    q, k, v, cu_q, cu_k = ref.make_varlen([777], [777], 4, 4, 128, torch.bfloat16)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    out_v = mfa.flash_attn_varlen_func(qd, kd, vd, cu_q.to(DEV), cu_k.to(DEV), 777, 777, causal=True)
+    out_d = mfa.flash_attn_func(qd[None], kd[None], vd[None], causal=True)[0]
+    torch.testing.assert_close(out_v, out_d, atol=0, rtol=0)
+
+
+def test_varlen_ragged_with_empty_sequences():
+    lq = [0, 1, 300, 0, 1000, 17, 0]
+    lk = [5, 0, 400, 0, 999, 17, 3]
+    q, k, v, cu_q, cu_k = ref.make_varlen(lq, lk, 4, 2, 64, torch.float16, seed=4)
+    out = mfa.flash_attn_varlen_func(q.to(DEV), k.to(DEV), v.to(DEV), cu_q.to(DEV), cu_k.to(DEV),
+                                     max(lq), max(lk), causal=True)
+    want = ref.flash_attn_varlen_func(q, k, v, cu_q, cu_k, causal=True)
+    check_close(out, want, torch.float16)
+
+
+def test_lse_and_combine_split_kv():
+    """Splitting keys across calls (k_pos_offset / lk_total) and merging with mfa_lse_combine
+    equals the unsplit forward."""
+    from mtlflashattn_b200 import _kernel, _lib
+
+    q, k, v = ref.make_qkv(1, 700, 1000, 4, 4, 128, torch.bfloat16, seed=12)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    bias = _kernel._BiasParams(0.0, -1, -1, None)
+    parts, lses = [], []
+    for a, b in ((0, 300), (300, 640), (640, 1000)):
+        o = torch.empty(1, 700, 4, 128, device=DEV, dtype=torch.float32)
+        lse = torch.empty(1, 4, 700, device=DEV, dtype=torch.float32)
+        _kernel.forward_bshd(qd, kd[:, a:b], vd[:, a:b], o, 1 / math.sqrt(128), True, bias,
+                             lse=lse, k_pos_offset=a, lk_total=1000)
+        parts.append(o)
+        lses.append(lse)
+    out = torch.empty(700, 4, 128, device=DEV, dtype=torch.bfloat16)
+    lse_out = torch.empty(4, 700, device=DEV, dtype=torch.float32)
+    rc = _lib.lse_combine([p.data_ptr() for p in parts], [l.data_ptr() for l in lses], 700, 4,
+                          128, out.data_ptr(), _lib.BF16, lse_out.data_ptr(),
+                          torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    want, want_lse = ref.attention_heads_second(qd.float().transpose(1, 2), kd.float().transpose(1, 2),
+                                                vd.float().transpose(1, 2), 1 / math.sqrt(128), True,
+                                                return_lse=True)
+    check_close(out, want[0].transpose(0, 1), torch.bfloat16)
+    fin = torch.isfinite(want_lse[0])
+    torch.testing.assert_close(lse_out[fin].cpu(), want_lse[0][fin].cpu(), atol=1e-3, rtol=1e-4)
+
+
+def test_api_errors_on_gpu():
+    q, k, v = ref.make_qkv(1, 16, 16, 1, 1, 160, torch.float16)
+    with pytest.raises(NotImplementedError):
+        mfa.flash_attn_func(q.to(DEV), k.to(DEV), v.to(DEV))
+    q, k, v = (t.to(DEV) for t in ref.make_qkv(1, 32, 32, 4, 4, 64, torch.float16))
+    with pytest.raises(ValueError):
+        mfa.flash_attn_func(q, k, v, softcap=-1.0)
+    with pytest.raises(ValueError):
+        mfa.flash_attn_func(q, k, v, alibi_slopes=torch.ones(3, device=DEV))
+    with pytest.raises(TypeError):
+        mfa.flash_attn_func(q, k, v, alibi_slopes=[0.5, 0.25, 0.125, 0.0625])
+    with pytest.raises(NotImplementedError):
+        mfa.flash_attn_func(q, k, v, dropout_p=0.1)
+    with pytest.raises(ValueError):
+        mfa.flash_attn_func(q, k[:, :, :3], v[:, :, :3])
+    q32 = q.float()
+    os.environ["MTLFLASHATTN_KERNEL"] = "tcgen05"
+    try:
+        with pytest.raises(RuntimeError):
+            mfa.flash_attn_func(q32, k.float(), v.float())
+    finally:
+        del os.environ["MTLFLASHATTN_KERNEL"]
