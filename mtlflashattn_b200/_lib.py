@@ -1,7 +1,7 @@
 """ctypes binding of libmfa.so (C ABI declared in include/mfa.h).
 
 The shared library is built in-tree by ``mtlflashattn_b200.build`` and loaded from this
-package's directory. Nothing here falls back to another implementation: if the library is
+package's directory (or from ``MTLFLASHATTN_LIB``, the path of another build of it). Nothing here falls back to another implementation: if the library is
 missing or a call fails, an exception is raised.
 """
 from __future__ import annotations
@@ -101,7 +101,7 @@ def load(path: str | None = None) -> ctypes.CDLL:
     with _lock:
         if _lib is not None:
             return _lib
-        p = path or LIB_PATH
+        p = path or os.environ.get("MTLFLASHATTN_LIB") or LIB_PATH
         if not os.path.exists(p):
             raise RuntimeError(
                 f"libmfa.so not found at {p}; build it with `python -m mtlflashattn_b200.build`"

@@ -115,7 +115,9 @@ __device__ __forceinline__ void store_row_chunk(const FwdArgs& a, void* row_ptr,
                                                 const float* vals, int n) {
   if (a.o_dtype == 2) {
     float* p = reinterpret_cast<float*>(row_ptr) + col0;
-    for (int i = 0; i < n; ++i) p[i] = vals[i];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < n) p[i] = vals[i];
     return;
   }
   uint16_t* p = reinterpret_cast<uint16_t*>(row_ptr) + col0;
@@ -133,13 +135,16 @@ __device__ __forceinline__ void store_row_chunk(const FwdArgs& a, void* row_ptr,
     for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
     return;
   }
-  for (int i = 0; i < n; ++i) {
-    if (a.o_dtype == 1) {
-      __nv_bfloat16 h = __float2bfloat16_rn(vals[i]);
-      p[i] = *reinterpret_cast<uint16_t*>(&h);
-    } else {
-      __half h = __float2half_rn(vals[i]);
-      p[i] = *reinterpret_cast<uint16_t*>(&h);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    if (i < n) {
+      if (a.o_dtype == 1) {
+        __nv_bfloat16 h = __float2bfloat16_rn(vals[i]);
+        p[i] = *reinterpret_cast<uint16_t*>(&h);
+      } else {
+        __half h = __float2half_rn(vals[i]);
+        p[i] = *reinterpret_cast<uint16_t*>(&h);
+      }
     }
   }
 }

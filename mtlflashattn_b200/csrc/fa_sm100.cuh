@@ -1,20 +1,31 @@
 // Flash-attention forward for B200 (sm_100a): TMA -> mbarrier ring -> tcgen05.mma with TMEM
-// accumulators -> fp32 online softmax in registers -> P back to TMEM -> P.V on tcgen05.
+// accumulators -> fp32 online softmax in registers -> P -> P.V on tcgen05.
 //
 // One CTA owns 256 query rows of one (batch, head) as two 128-row tiles (t = 0, 1) and streams
 // the key/value blocks (128 keys each) that any of those rows may attend.
 //
-//   warps 0-3  softmax for tile 0   (TMEM lanes 0-127, one query row per thread)
-//   warps 4-7  softmax for tile 1
-//   warp  8    TMA producer: Q tiles once, then K_j, V_j into a shared ring of NSLOT slots
-//   warp  9    TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 0-3   softmax for tile 0   (TMEM lanes 0-127, one query row per thread)
+//   warps 4-7   softmax for tile 1
+//   warp  8     TMA producer: Q tiles once, then K_j, V_j into a shared ring of NSLOT slots
+//   warp  9     TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 10-11 idle (they complete the third warpgroup, whose registers go to the softmax)
+// Registers: launched at 168 per thread (384 threads); the softmax warpgroups raise theirs to
+// kSoftmaxRegs and the producer/MMA warpgroup lowers its to kOtherRegs (setmaxnreg), so each
+// softmax thread keeps a full 128-column row of S in registers without spilling.
 //
-// TMEM columns (512 allocated): S0 [0,128) S1 [128,256) O0 [256,256+DP) O1 [256+DP,256+2DP).
-// P_t (16-bit, two per column) overwrites the first 64 columns of S_t once S_t is in registers.
-// The MMA warp issues, per key block j:  PV0_j, S0_{j+1}, PV1_j, S1_{j+1}.  tcgen05 MMAs of
-// one thread execute in issue order, so S_t(j+1) never overwrites P_t(j) before PV_t(j) read it,
-// and the commit that publishes S_t(j+1) also covers PV_t(j); that is what lets the softmax
-// warps rescale O_t in place right after they see S_t(j+1).
+// TMEM columns (512 allocated): S0 [0,128) S1 [128,256) O0 [256,256+DP) O1 [256+DP,256+2DP),
+// and for DP = 64 the 16-bit probabilities P0 [384,448) P1 [448,512) (two per column). For
+// DP = 128 TMEM is full, so P_t goes to a 32 KB shared-memory tile in the 128-byte-swizzled
+// K-major layout the MMA reads.
+//
+// Per tile t and key block j the handshakes are:
+//   s_full[t]   MMA -> softmax   S_t(j) = Q_t K_j^T is in TMEM
+//   s_free[t]   softmax -> MMA   S_t(j) is in registers; the MMA may write S_t(j+1)
+//   p_full[t]   softmax -> MMA   P_t(j) written and O_t rescaled; the MMA may run P_t(j) V_j
+//   pv_done[t]  MMA -> softmax   P_t(j) V_j complete; O_t idle and P_t reusable
+// Because S is released as soon as it is loaded, S_t(j+1) runs on the tensor cores while the
+// softmax of block j is still computing. The MMA warp issues whichever of the four streams
+// (S0, S1, PV0, PV1) is ready, polling the barriers without blocking on any one of them.
 //
 // Semantics follow the reference's chunked-fp32 tier (metal_flash_attn/_kernel.py:1165-1208):
 // scale, softcap, ALiBi, bottom-right causal and sliding window, fully masked rows -> 0.
@@ -35,7 +46,12 @@ namespace sm100 {
 
 constexpr int BM = 128;  // query rows per tile (TMEM lanes)
 constexpr int BN = 128;  // keys per block
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
+constexpr int kLaunchRegs = 168;  // 65536 / 384 rounded down to a multiple of 8
+constexpr int kSoftmaxRegs = 224;
+constexpr int kOtherRegs = 56;
+static_assert(2 * 128 * kSoftmaxRegs + 128 * kOtherRegs <= kThreads * kLaunchRegs,
+              "setmaxnreg split exceeds the launch register budget");
 
 template <int DP>
 struct Cfg {
@@ -43,12 +59,16 @@ struct Cfg {
   static constexpr uint32_t CHUNK = 128u * 128u;         // one chunk of 128 rows: 16 KB
   static constexpr uint32_t TILE = NCH * CHUNK;          // Q tile or K / V block
   static constexpr int NSLOT = DP == 128 ? 3 : 6;        // K/V ring depth
-  static constexpr uint32_t BAR_OFF = 2 * TILE + NSLOT * TILE;
+  static constexpr bool P_SMEM = DP == 128;              // P tiles in shared memory
+  static constexpr uint32_t P_TILE = 2 * CHUNK;          // 128 rows x 128 keys, 16-bit
+  static constexpr uint32_t P_OFF = 2 * TILE + NSLOT * TILE;
+  static constexpr uint32_t BAR_OFF = P_OFF + (P_SMEM ? 2 * P_TILE : 0);
   static constexpr uint32_t SMEM = BAR_OFF + 256 + 1024;  // + barriers + alignment slack
+  static constexpr uint32_t TMEM_P = 384;                 // P columns when !P_SMEM
 };
 
 // Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.
-// K-major tiles (Q, K): SBO = 1024 B between 8-row groups; LBO unused (1).
+// K-major tiles (Q, K, P): SBO = 1024 B between 8-row groups; LBO unused (1).
 // MN-major tile (V as the B operand of P.V): LBO = 16 KB between 64-column chunks,
 // SBO = 1024 B between 8-key groups.
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -64,7 +84,15 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 
 }  // namespace sm100
 
-template <int DP, bool kBF16, bool kGeneral>
+// kEmu: of every 8 pairs of probabilities, how many are computed with exp2_poly2 on the FMA
+// pipe instead of MUFU.EX2 (balances the two pipes).
+#ifndef MFA_EMU64
+#define MFA_EMU64 0
+#endif
+#ifndef MFA_EMU128
+#define MFA_EMU128 0
+#endif
+template <int DP, bool kBF16, bool kGeneral, int kEmu = (DP == 64 ? MFA_EMU64 : MFA_EMU128)>
 __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_constant__ Sm100Args args) {
   using namespace sm100;
   using C = Cfg<DP>;
@@ -75,14 +103,16 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
   uint8_t* sb = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* sQ = sb;
   uint8_t* sKV = sb + 2 * C::TILE;
+  uint8_t* sP = sb + C::P_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sb + C::BAR_OFF);
   uint64_t* q_full = bars;                 // [2]
   uint64_t* kv_full = bars + 2;            // [NSLOT]
   uint64_t* kv_empty = kv_full + C::NSLOT; // [NSLOT]
   uint64_t* s_full = kv_empty + C::NSLOT;  // [2]
-  uint64_t* p_full = s_full + 2;           // [2]
-  uint64_t* o_full = p_full + 2;           // [2]
-  uint64_t* mma_done = o_full + 2;         // [1]
+  uint64_t* s_free = s_full + 2;           // [2]
+  uint64_t* p_full = s_free + 2;           // [2]
+  uint64_t* pv_done = p_full + 2;          // [2]
+  uint64_t* mma_done = pv_done + 2;        // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -99,11 +129,9 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
   if (r0 >= sv.lq) return;  // whole CTA leaves before touching barriers or TMEM
 
   const int r_last = min(r0 + 2 * BM, sv.lq) - 1;
-  const KeyRange kr_first = key_range(a, sv, r0);
-  const KeyRange kr_last = key_range(a, sv, r_last);
-  // union of the rows' intervals: lo is nondecreasing in the row, hi too
-  const int klo = kr_first.lo;
-  const int khi = kr_last.hi;
+  // union of the rows' key intervals: lo and hi are nondecreasing in the row
+  const int klo = key_range(a, sv, r0).lo;
+  const int khi = key_range(a, sv, r_last).hi;
   const int jb = klo / BN;
   const int n = khi > klo ? (khi + BN - 1) / BN - jb : 0;
 
@@ -119,8 +147,9 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
+      mbar_init(&s_free[t], 4);
       mbar_init(&p_full[t], 4);
-      mbar_init(&o_full[t], 1);
+      mbar_init(&pv_done[t], 1);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -140,7 +169,10 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  if (warp >= 10) {
+    regs_dec<kOtherRegs>();  // idle warps of the producer/MMA warpgroup
+  } else if (warp == 8) {
+    regs_dec<kOtherRegs>();
     // ------------------------------------------------------------ TMA producer
     if (n > 0) {
       const int qrow = sv.q0 + r0;
@@ -169,91 +201,83 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
       }
     }
   } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
-    constexpr uint32_t kIdQK = idesc_f16(kBF16, BM, BN, false);
-    constexpr uint32_t kIdPV = idesc_f16(kBF16, BM, DP, true);
-    const uint32_t sQa = smem_u32(sQ);
-    const uint32_t sKVa = smem_u32(sKV);
-    bool ok = true;
-    auto qk = [&](int t, int slot) {  // S_t = Q_t K^T
+    // ------------------------------------------------------------ MMA issuer (one thread)
+    regs_dec<kOtherRegs>();
+    if (n > 0 && lane == 0) {
+      constexpr uint32_t kIdQK = idesc_f16(kBF16, BM, BN, false);
+      constexpr uint32_t kIdPV = idesc_f16(kBF16, BM, DP, true);
+      const uint32_t sQa = smem_u32(sQ);
+      const uint32_t sKVa = smem_u32(sKV);
+      const uint32_t sPa = smem_u32(sP);
+      bool ok = mbar_wait(&q_full[0], 0, abort_flag) && mbar_wait(&q_full[1], 0, abort_flag);
+      tc_fence_after();
+      int sj[2] = {0, 0};  // next block whose S_t is to be issued
+      int pj[2] = {0, 0};  // next block whose P_t V is to be issued
+      uint64_t idle_since = 0;
+      uint32_t idle_polls = 0;
+      while (ok && (pj[0] < n || pj[1] < n)) {
+        bool progressed = false;
 #pragma unroll
-      for (int k = 0; k < DP / 16; ++k) {
-        const uint32_t koff = (k >> 2) * C::CHUNK + (k & 3) * 32;
-        mma_ss(tmem + 128u * t, desc_sw128(sQa + t * C::TILE + koff, 16, 1024),
-               desc_sw128(sKVa + slot * C::TILE + koff, 16, 1024), kIdQK, k > 0);
-      }
-    };
-    auto pv = [&](int t, int slot, bool acc) {  // O_t (+)= P_t V
+        for (int t = 0; t < 2; ++t) {
+          const int j = sj[t];
+          const int itK = 2 * j;
+          if (j < n && (j == 0 || mbar_test(&s_free[t], (uint32_t)(j - 1) & 1u)) &&
+              mbar_test(&kv_full[itK % C::NSLOT], (uint32_t)(itK / C::NSLOT) & 1u)) {
+            tc_fence_after();
+            const uint32_t kb_addr = sKVa + (itK % C::NSLOT) * C::TILE;
 #pragma unroll
-      for (int k = 0; k < BN / 16; ++k)
-        mma_ts(tmem + 256u + DP * t, tmem + 128u * t + k * 8, desc_sw128(sKVa + slot * C::TILE + k * 2048, C::CHUNK, 1024),
-               kIdPV, (acc || k > 0) ? 1u : 0u);
-    };
-    if (n > 0) {
-      ok = mbar_wait(&q_full[0], 0, abort_flag) && mbar_wait(&q_full[1], 0, abort_flag);
-      ok = __all_sync(kFull, ok);
-      int slotK = 0;
-      if (ok) {
-        ok = __all_sync(kFull, mbar_wait(&kv_full[0], 0, abort_flag));
-      }
-      if (ok) {
-        tc_fence_after();
-        if (lane == 0) {
-          qk(0, 0);
-          tc_commit(&s_full[0]);
-          qk(1, 0);
-          tc_commit(&s_full[1]);
-          tc_commit(&kv_empty[0]);
-        }
-        __syncwarp();
-      }
-      for (int j = 0; j < n && ok; ++j) {
-        const int itV = 2 * j + 1;
-        const int slotV = itV % C::NSLOT;
-        ok = mbar_wait(&kv_full[slotV], (uint32_t)(itV / C::NSLOT) & 1u, abort_flag);
-        ok = __all_sync(kFull, ok && mbar_wait(&p_full[0], (uint32_t)j & 1u, abort_flag));
-        if (!ok) break;
-        tc_fence_after();
-        if (lane == 0) {
-          pv(0, slotV, j > 0);
-          if (j == n - 1) tc_commit(&o_full[0]);
-        }
-        __syncwarp();
-        const bool more = j + 1 < n;
-        if (more) {
-          const int itK = 2 * j + 2;
-          slotK = itK % C::NSLOT;
-          ok = __all_sync(kFull, mbar_wait(&kv_full[slotK], (uint32_t)(itK / C::NSLOT) & 1u, abort_flag));
-          if (!ok) break;
-          tc_fence_after();
-          if (lane == 0) {
-            qk(0, slotK);
-            tc_commit(&s_full[0]);
+            for (int k = 0; k < DP / 16; ++k) {  // S_t = Q_t K_j^T
+              const uint32_t koff = (k >> 2) * C::CHUNK + (k & 3) * 32;
+              mma_ss(tmem + 128u * t, desc_sw128(sQa + t * C::TILE + koff, 16, 1024),
+                     desc_sw128(kb_addr + koff, 16, 1024), kIdQK, k > 0);
+            }
+            tc_commit(&s_full[t]);
+            if (sj[1 - t] > j) tc_commit(&kv_empty[itK % C::NSLOT]);  // both tiles used K_j
+            sj[t] = j + 1;
+            progressed = true;
           }
-          __syncwarp();
-        }
-        ok = __all_sync(kFull, mbar_wait(&p_full[1], (uint32_t)j & 1u, abort_flag));
-        if (!ok) break;
-        tc_fence_after();
-        if (lane == 0) {
-          pv(1, slotV, j > 0);
-          tc_commit(&kv_empty[slotV]);
-          if (j == n - 1) tc_commit(&o_full[1]);
-          if (more) {
-            qk(1, slotK);
-            tc_commit(&s_full[1]);
-            tc_commit(&kv_empty[slotK]);
+          const int jp = pj[t];
+          const int itV = 2 * jp + 1;
+          if (jp < n && jp < sj[t] && mbar_test(&p_full[t], (uint32_t)jp & 1u) &&
+              mbar_test(&kv_full[itV % C::NSLOT], (uint32_t)(itV / C::NSLOT) & 1u)) {
+            tc_fence_after();
+            const uint32_t vb_addr = sKVa + (itV % C::NSLOT) * C::TILE;
+#pragma unroll
+            for (int k = 0; k < BN / 16; ++k) {  // O_t (+)= P_t V_j
+              const uint64_t bdesc = desc_sw128(vb_addr + k * 2048, C::CHUNK, 1024);
+              const uint32_t acc = (jp > 0 || k > 0) ? 1u : 0u;
+              if constexpr (C::P_SMEM) {
+                const uint32_t poff = t * C::P_TILE + (k >> 2) * C::CHUNK + (k & 3) * 32;
+                mma_ss(tmem + 256u + DP * t, desc_sw128(sPa + poff, 16, 1024), bdesc, kIdPV, acc);
+              } else {
+                mma_ts(tmem + 256u + DP * t, tmem + C::TMEM_P + 64u * t + k * 8, bdesc, kIdPV, acc);
+              }
+            }
+            tc_commit(&pv_done[t]);
+            if (pj[1 - t] > jp) tc_commit(&kv_empty[itV % C::NSLOT]);  // both tiles used V_j
+            pj[t] = jp + 1;
+            progressed = true;
           }
         }
-        __syncwarp();
+        if (progressed) {
+          idle_polls = 0;
+        } else if (++idle_polls == 1) {
+          idle_since = globaltimer_ns();
+        } else if ((idle_polls & 255u) == 0) {
+          if (*abort_flag || globaltimer_ns() - idle_since > kWaitTimeoutNs) {
+            *abort_flag = 1;
+            ok = false;
+          }
+        }
       }
       // Drain: every MMA issued above has completed before TMEM is released.
-      if (lane == 0) tc_commit(mma_done);
-      __syncwarp();
+      tc_commit(mma_done);
       if (!mbar_wait_drain(mma_done, 0)) *abort_flag = 1;
     }
+    __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax warpgroups
+    regs_inc<kSoftmaxRegs>();
     const int t = warp >> 2;        // tile
     const int wq = warp & 3;        // TMEM lane quarter
     const int rt = wq * 32 + lane;  // row within tile
@@ -261,16 +285,23 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
     const uint32_t tS = tmem + lane_base + t * 128;
     const uint32_t tO = tmem + lane_base + 256 + t * DP;
+    const uint32_t tP = tmem + lane_base + C::TMEM_P + t * 64;
+    uint8_t* sProw = sP + t * C::P_TILE + rt * 128;  // this row inside the swizzled P tile
     const KeyRange kr = key_range(a, sv, row);
     // tile-uniform interval extremes for the "block needs no mask" test
     const int tile_lo_max = key_range(a, sv, (int64_t)r0 + t * BM + BM - 1).lo;
     const int tile_hi_min = key_range(a, sv, (int64_t)r0 + t * BM).hi;
     constexpr float kLog2e = 1.4426950408889634f;
-    const float c = kGeneral ? 1.f : a.scale * kLog2e;  // multiplies x to reach log2 units
-    float slope = 0.f;
-    if (kGeneral && a.alibi != nullptr) slope = a.alibi[(int64_t)b * a.Hq + h];
-    const float centre = (float)(row + sv.off);
+    // x (the values kept in registers) times c is the logit in log2 units
+    const float c = kGeneral ? 1.f : a.scale * kLog2e;
+    float slope_l2 = 0.f;  // ALiBi slope in log2 units
+    if (kGeneral && a.alibi != nullptr) slope_l2 = a.alibi[(int64_t)b * a.Hq + h] * kLog2e;
     const float cap = a.softcap;
+    // softcap: x = cap*log2e*tanh(y) with tanh(y) = 1 - 2/(2^(2*log2e*y) + 1), y = s*scale/cap
+    const float sc_in = cap > 0.f ? a.scale * 2.f * kLog2e / cap : 0.f;
+    const float sc_a = cap * kLog2e, sc_b = -2.f * cap * kLog2e;
+    const float pl_scale = a.scale * kLog2e;  // no softcap: x = s*scale*log2e
+    const float centre = (float)(row + sv.off);
 
     float m_used = -INFINITY;  // in x units
     float l = 0.f;
@@ -288,19 +319,44 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
       tmem_ld_tie32(r + 32);
       tmem_ld_tie32(r + 64);
       tmem_ld_tie32(r + 96);
+      // S_t is in registers: hand the TMEM columns back for S_t(j+1)
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[t]);
       float x[128];
       const int c0 = (jb + j) * BN;
       const bool need_mask = (c0 < tile_lo_max) || (c0 + BN > tile_hi_min);
       if constexpr (kGeneral) {
-        // x = log2(e) * (softcap(s * scale) - slope * |centre - key|), masked -> -inf
+        // x = log2(e) * (softcap(s * scale) - slope * |centre - key|)
+        const float d0 = centre - (float)(c0 + a.k_pos_offset);  // centre - key for i = 0
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          float s = __uint_as_float(r[i]) * a.scale;
-          if (cap > 0.f) s = cap * tanh_exp2(s / cap);
-          const int kl = c0 + i;
-          s -= slope * fabsf(centre - (float)(kl + a.k_pos_offset));
-          x[i] = s * kLog2e;
-          if (need_mask && (kl < kr.lo || kl >= kr.hi)) x[i] = -INFINITY;
+        for (int i = 0; i < 128; i += 2) {
+          uint64_t s2 = f2pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+          uint64_t x2;
+          if (cap > 0.f) {
+            float ya, yb;
+            f2unpack(fmul2(s2, f2pack(sc_in, sc_in)), ya, yb);
+            ya = fminf(fmaxf(ya, -43.f), 43.f);  // |tanh| = 1 in fp32 beyond 2*log2e*15
+            yb = fminf(fmaxf(yb, -43.f), 43.f);
+            const uint64_t e2 = fadd2(f2pack(ex2(ya), ex2(yb)), f2pack(1.f, 1.f));
+            float ea, eb;
+            f2unpack(e2, ea, eb);
+            x2 = ffma2(f2pack(rcp(ea), rcp(eb)), f2pack(sc_b, sc_b), f2pack(sc_a, sc_a));
+          } else {
+            x2 = fmul2(s2, f2pack(pl_scale, pl_scale));
+          }
+          if (slope_l2 != 0.f) {
+            float da = fabsf(d0 - (float)i), db = fabsf(d0 - (float)(i + 1));
+            x2 = ffma2(f2pack(da, db), f2pack(-slope_l2, -slope_l2), x2);
+          }
+          f2unpack(x2, x[i], x[i + 1]);
+        }
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i) {
+            const int kl = c0 + i;
+            if (kl < kr.lo || kl >= kr.hi) x[i] = -INFINITY;
+          }
         }
       } else {
         if (need_mask) {
@@ -314,27 +370,38 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
           for (int i = 0; i < 128; ++i) x[i] = __uint_as_float(r[i]);
         }
       }
-      float mx0 = x[0], mx1 = x[1], mx2 = x[2], mx3 = x[3];
+      float mx0 = fmax3(x[0], x[1], x[2]), mx1 = fmax3(x[3], x[4], x[5]);
+      float mx2 = fmax3(x[6], x[7], x[8]), mx3 = fmax3(x[9], x[10], x[11]);
 #pragma unroll
-      for (int i = 4; i < 128; i += 4) {
-        mx0 = fmaxf(mx0, x[i]);
-        mx1 = fmaxf(mx1, x[i + 1]);
-        mx2 = fmaxf(mx2, x[i + 2]);
-        mx3 = fmaxf(mx3, x[i + 3]);
+      for (int i = 12; i < 124; i += 8) {
+        mx0 = fmax3(mx0, x[i], x[i + 1]);
+        mx1 = fmax3(mx1, x[i + 2], x[i + 3]);
+        mx2 = fmax3(mx2, x[i + 4], x[i + 5]);
+        mx3 = fmax3(mx3, x[i + 6], x[i + 7]);
       }
-      const float m_new = fmaxf(m_used, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)));
+      mx0 = fmax3(mx0, x[124], x[125]);
+      mx1 = fmax3(mx1, x[126], x[127]);
+      const float m_new = fmax3(m_used, fmaxf(mx0, mx1), fmaxf(mx2, mx3));
       const bool grow = (m_new - m_used) * c > 8.f;  // false when both are -inf (NaN compare)
+      // P_t and O_t are in use by P_t(j-1) V_{j-1} until pv_done
+      if (j > 0) {
+        ok = __all_sync(kFull, mbar_wait(&pv_done[t], (uint32_t)(j - 1) & 1u, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+      }
       if (__any_sync(kFull, grow)) {
         const float factor = (m_used == -INFINITY) ? 0.f : ex2((m_used - m_new) * c);
         if (j > 0) {
-          // O_t is idle here: the commit that published S_t(j) also covered PV_t(j-1).
 #pragma unroll 1
           for (int cc = 0; cc < DP; cc += 32) {
             uint32_t o[32];
             tmem_ld32(tO + cc, o);
             tmem_ld_wait32(o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+            for (int i = 0; i < 32; i += 2) {
+              const uint64_t v2 = fmul2(u2pack(o[i], o[i + 1]), f2pack(factor, factor));
+              u2unpack(v2, o[i], o[i + 1]);
+            }
             tmem_st32(tO + cc, o);
           }
         }
@@ -342,27 +409,56 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
         m_used = m_new;
       }
       const float ref = (m_used == -INFINITY) ? 0.f : m_used * c;
-      float l0 = 0.f, l1 = 0.f;
+      // p = 2^(x*c - ref): a fraction kEmu/8 of the pairs on the FMA pipe, the rest on MUFU
+      const uint64_t c2 = f2pack(c, c), nref2 = f2pack(-ref, -ref);
+      uint64_t acc0 = f2pack(0.f, 0.f), acc1 = acc0;
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {  // 32 keys -> 16 packed columns per store
+      for (int cc = 0; cc < 4; ++cc) {  // 32 keys -> 16 packed words per step
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2(fmaf(x[32 * cc + 2 * i], c, -ref));
-          const float p1 = ex2(fmaf(x[32 * cc + 2 * i + 1], c, -ref));
-          l0 += p0;
-          l1 += p1;
+          const int e = 32 * cc + 2 * i;
+          const uint64_t t2 = ffma2(f2pack(x[e], x[e + 1]), c2, nref2);
+          uint64_t p2;
+          if ((i & 7) < kEmu) {
+            p2 = exp2_poly2(t2);
+          } else {
+            float ta, tb;
+            f2unpack(t2, ta, tb);
+            p2 = f2pack(ex2(ta), ex2(tb));
+          }
+          if (i & 1) acc1 = fadd2(acc1, p2); else acc0 = fadd2(acc0, p2);
+          float p0, p1;
+          f2unpack(p2, p0, p1);
           pk[i] = pack2<kBF16>(p0, p1);
         }
-        tmem_st16(tS + 16 * cc, pk);
+        if constexpr (C::P_SMEM) {
+          // keys 32cc..32cc+31 = four 16-byte units of the row in 128B-swizzled chunk cc/2
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int u = (4 * cc + q) & 7;
+            uint4* dst = reinterpret_cast<uint4*>(sProw + (cc >> 1) * C::CHUNK + ((u ^ (rt & 7)) << 4));
+            *dst = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          }
+        } else {
+          tmem_st16(tP + 16 * cc, pk);
+        }
       }
-      l += l0 + l1;
-      tmem_st_wait();
+      float la, lb;
+      f2unpack(fadd2(acc0, acc1), la, lb);
+      l += la + lb;
+      if constexpr (C::P_SMEM) {
+        fence_proxy_async_smem();
+      } else {
+        tmem_st_wait();
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
     }
-    if (ok && n > 0) ok = __all_sync(kFull, mbar_wait(&o_full[t], 0, abort_flag));
+    if (ok && n > 0) {
+      ok = __all_sync(kFull, mbar_wait(&pv_done[t], (uint32_t)(n - 1) & 1u, abort_flag));
+    }
     if (ok) {
       tc_fence_after();
       const bool store = row < sv.lq;

@@ -104,8 +104,8 @@ int validate(const mfa_fwd_params* p) {
   if (!varlen && (p->Lq < 0 || p->Lk < 0)) return MFA_ERR_INVALID;
   if (varlen && p->max_lq < 0) return MFA_ERR_INVALID;
   if (p->B == 0 || (!varlen && p->Lq == 0) || (varlen && p->max_lq == 0)) return MFA_OK;
-  if (p->q == nullptr || p->k == nullptr || p->v == nullptr || p->o == nullptr)
-    return MFA_ERR_INVALID;
+  if (p->q == nullptr || p->o == nullptr) return MFA_ERR_INVALID;
+  if ((p->k == nullptr || p->v == nullptr) && p->Lk > 0) return MFA_ERR_INVALID;
   return MFA_OK;
 }
 
@@ -206,6 +206,15 @@ template <int DP, bool BF16, bool GEN>
 int launch_sm100(const Sm100Args& args, int dev, int64_t grid, cudaStream_t st) {
   auto k = fa_fwd_sm100<DP, BF16, GEN>;
   const int smem = (int)sm100::Cfg<DP>::SMEM;
+  // The kernel re-splits its registers with setmaxnreg assuming exactly kLaunchRegs per thread
+  // at launch; a build that launched with fewer would make setmaxnreg.inc wait forever.
+  static int launch_regs = -1;
+  if (launch_regs < 0) {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) return MFA_ERR_CUDA;
+    launch_regs = fa.numRegs;
+  }
+  if (launch_regs != sm100::kLaunchRegs) return MFA_ERR_UNSUPPORTED;
   if (ensure_smem(k, dev, smem) != cudaSuccess) return MFA_ERR_CUDA;
   k<<<(unsigned)grid, sm100::kThreads, smem, st>>>(args);
   return MFA_OK;

@@ -78,6 +78,24 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
   }
 }
 
+// Non-blocking probe: has the phase with the given parity completed?
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy reads
+// (tcgen05.mma operands, TMA stores).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -189,12 +207,101 @@ __device__ __forceinline__ void tmem_st_wait() {
 #undef MFA_W8
 #undef MFA_P8
 
+// ---------------------------------------------------------------- register budget
+// Re-balance the per-thread register budget between warpgroups (all 4 warps of a warpgroup
+// execute the same instruction). The sum over warpgroups must not exceed the launch budget.
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---------------------------------------------------------------- math
 // Hardware base-2 exponential (MUFU.EX2), flush-to-zero; exp2(-inf) = 0.
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+// Hardware reciprocal (MUFU.RCP), flush-to-zero.
+__device__ __forceinline__ float rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// ---------------------------------------------------------------- packed fp32 pairs (f32x2)
+// sm_100 executes add/mul/fma on two fp32 lanes per instruction; a pair lives in a 64-bit
+// register as {lo, hi}.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ void u2unpack(uint64_t r, uint32_t& lo, uint32_t& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t u2pack(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^t for a pair, on the FMA pipe instead of MUFU. Range reduction t = n + f with
+// n = round(t) (adding 1.5 * 2^23 leaves n in the low mantissa bits), f in [-1/2, 1/2];
+// 2^f from a degree-3 polynomial whose coefficients minimise the maximum relative error on
+// [-1/2, 1/2] (Remez exchange, derived by fit_exp2_poly.py in this directory: max relative
+// error 7.5e-5, below the 2^-9 / 2^-11 rounding of the bf16 / fp16 probabilities it feeds);
+// 2^n is added to the exponent field as an integer. t is clamped at -127 (this maps -inf
+// there too); a result whose exponent field would underflow is set to +0 by an integer max, so
+// masked logits give exactly 0 as MUFU.EX2 does.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t t) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261113f, c3 = 0.05517167f;
+  float a, b;
+  f2unpack(t, a, b);
+  const uint64_t tc = f2pack(fmaxf(a, -127.f), fmaxf(b, -127.f));
+  const uint64_t r = fadd2(tc, f2pack(kRound, kRound));
+  const uint64_t f = fsub2(tc, fsub2(r, f2pack(kRound, kRound)));
+  uint64_t p = ffma2(f, f2pack(c3, c3), f2pack(c2, c2));
+  p = ffma2(p, f, f2pack(c1, c1));
+  p = ffma2(p, f, f2pack(c0, c0));
+  uint32_t pl, ph, rl, rh;
+  u2unpack(p, pl, ph);
+  u2unpack(r, rl, rh);
+  return u2pack((uint32_t)max((int)(pl + (rl << 23)), 0), (uint32_t)max((int)(ph + (rh << 23)), 0));
 }
 
 }  // namespace mfa
