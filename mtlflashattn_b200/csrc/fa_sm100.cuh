@@ -13,19 +13,14 @@
 // kSoftmaxRegs and the producer/MMA warpgroup lowers its to kOtherRegs (setmaxnreg), so each
 // softmax thread keeps a full 128-column row of S in registers without spilling.
 //
-// TMEM columns (512 allocated): S0 [0,128) S1 [128,256) O0 [256,256+DP) O1 [256+DP,256+2DP),
-// and for DP = 64 the 16-bit probabilities P0 [384,448) P1 [448,512) (two per column). For
-// DP = 128 TMEM is full, so P_t goes to a 32 KB shared-memory tile in the 128-byte-swizzled
-// K-major layout the MMA reads.
-//
-// Per tile t and key block j the handshakes are:
-//   s_full[t]   MMA -> softmax   S_t(j) = Q_t K_j^T is in TMEM
-//   s_free[t]   softmax -> MMA   S_t(j) is in registers; the MMA may write S_t(j+1)
-//   p_full[t]   softmax -> MMA   P_t(j) written and O_t rescaled; the MMA may run P_t(j) V_j
-//   pv_done[t]  MMA -> softmax   P_t(j) V_j complete; O_t idle and P_t reusable
-// Because S is released as soon as it is loaded, S_t(j+1) runs on the tensor cores while the
-// softmax of block j is still computing. The MMA warp issues whichever of the four streams
-// (S0, S1, PV0, PV1) is ready, polling the barriers without blocking on any one of them.
+// TMEM columns (512 allocated): S0 [0,128) S1 [128,256) O0 [256,256+DP) O1 [256+DP,256+2DP).
+// P_t (16-bit, two per column) overwrites the first 64 columns of S_t once S_t is in registers.
+// The MMA warp issues, per key block j:  PV0_j, S0_{j+1}, PV1_j, S1_{j+1}.  tcgen05 MMAs of
+// one thread execute in issue order, so S_t(j+1) never overwrites P_t(j) before PV_t(j) read it,
+// and the commit that publishes S_t(j+1) also covers PV_t(j); that is what lets the softmax
+// warps rescale O_t in place right after they see S_t(j+1). (A variant that released S_t to the
+// MMA as soon as it was in registers, with P in separate TMEM columns or shared memory and an
+// event-driven issuer, measured 5-20% slower on every BASELINE configuration.)
 //
 // Semantics follow the reference's chunked-fp32 tier (metal_flash_attn/_kernel.py:1165-1208):
 // scale, softcap, ALiBi, bottom-right causal and sliding window, fully masked rows -> 0.
@@ -48,8 +43,8 @@ constexpr int BM = 128;  // query rows per tile (TMEM lanes)
 constexpr int BN = 128;  // keys per block
 constexpr int kThreads = 384;
 constexpr int kLaunchRegs = 168;  // 65536 / 384 rounded down to a multiple of 8
-constexpr int kSoftmaxRegs = 224;
-constexpr int kOtherRegs = 56;
+constexpr int kSoftmaxRegs = 208;
+constexpr int kOtherRegs = 88;
 static_assert(2 * 128 * kSoftmaxRegs + 128 * kOtherRegs <= kThreads * kLaunchRegs,
               "setmaxnreg split exceeds the launch register budget");
 
@@ -59,16 +54,12 @@ struct Cfg {
   static constexpr uint32_t CHUNK = 128u * 128u;         // one chunk of 128 rows: 16 KB
   static constexpr uint32_t TILE = NCH * CHUNK;          // Q tile or K / V block
   static constexpr int NSLOT = DP == 128 ? 3 : 6;        // K/V ring depth
-  static constexpr bool P_SMEM = DP == 128;              // P tiles in shared memory
-  static constexpr uint32_t P_TILE = 2 * CHUNK;          // 128 rows x 128 keys, 16-bit
-  static constexpr uint32_t P_OFF = 2 * TILE + NSLOT * TILE;
-  static constexpr uint32_t BAR_OFF = P_OFF + (P_SMEM ? 2 * P_TILE : 0);
+  static constexpr uint32_t BAR_OFF = 2 * TILE + NSLOT * TILE;
   static constexpr uint32_t SMEM = BAR_OFF + 256 + 1024;  // + barriers + alignment slack
-  static constexpr uint32_t TMEM_P = 384;                 // P columns when !P_SMEM
 };
 
 // Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.
-// K-major tiles (Q, K, P): SBO = 1024 B between 8-row groups; LBO unused (1).
+// K-major tiles (Q, K): SBO = 1024 B between 8-row groups; LBO unused (1).
 // MN-major tile (V as the B operand of P.V): LBO = 16 KB between 64-column chunks,
 // SBO = 1024 B between 8-key groups.
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -103,16 +94,14 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
   uint8_t* sb = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* sQ = sb;
   uint8_t* sKV = sb + 2 * C::TILE;
-  uint8_t* sP = sb + C::P_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sb + C::BAR_OFF);
   uint64_t* q_full = bars;                 // [2]
   uint64_t* kv_full = bars + 2;            // [NSLOT]
   uint64_t* kv_empty = kv_full + C::NSLOT; // [NSLOT]
   uint64_t* s_full = kv_empty + C::NSLOT;  // [2]
-  uint64_t* s_free = s_full + 2;           // [2]
-  uint64_t* p_full = s_free + 2;           // [2]
-  uint64_t* pv_done = p_full + 2;          // [2]
-  uint64_t* mma_done = pv_done + 2;        // [1]
+  uint64_t* p_full = s_full + 2;           // [2]
+  uint64_t* o_full = p_full + 2;           // [2]
+  uint64_t* mma_done = o_full + 2;         // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -147,9 +136,8 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&s_free[t], 4);
       mbar_init(&p_full[t], 4);
-      mbar_init(&pv_done[t], 1);
+      mbar_init(&o_full[t], 1);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -208,66 +196,58 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
       constexpr uint32_t kIdPV = idesc_f16(kBF16, BM, DP, true);
       const uint32_t sQa = smem_u32(sQ);
       const uint32_t sKVa = smem_u32(sKV);
-      const uint32_t sPa = smem_u32(sP);
-      bool ok = mbar_wait(&q_full[0], 0, abort_flag) && mbar_wait(&q_full[1], 0, abort_flag);
-      tc_fence_after();
-      int sj[2] = {0, 0};  // next block whose S_t is to be issued
-      int pj[2] = {0, 0};  // next block whose P_t V is to be issued
-      uint64_t idle_since = 0;
-      uint32_t idle_polls = 0;
-      while (ok && (pj[0] < n || pj[1] < n)) {
-        bool progressed = false;
+      auto qk = [&](int t, int it) {  // S_t = Q_t K^T, K in ring item `it`
+        const uint32_t kb_addr = sKVa + (it % C::NSLOT) * C::TILE;
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          const int j = sj[t];
-          const int itK = 2 * j;
-          if (j < n && (j == 0 || mbar_test(&s_free[t], (uint32_t)(j - 1) & 1u)) &&
-              mbar_test(&kv_full[itK % C::NSLOT], (uint32_t)(itK / C::NSLOT) & 1u)) {
-            tc_fence_after();
-            const uint32_t kb_addr = sKVa + (itK % C::NSLOT) * C::TILE;
-#pragma unroll
-            for (int k = 0; k < DP / 16; ++k) {  // S_t = Q_t K_j^T
-              const uint32_t koff = (k >> 2) * C::CHUNK + (k & 3) * 32;
-              mma_ss(tmem + 128u * t, desc_sw128(sQa + t * C::TILE + koff, 16, 1024),
-                     desc_sw128(kb_addr + koff, 16, 1024), kIdQK, k > 0);
-            }
-            tc_commit(&s_full[t]);
-            if (sj[1 - t] > j) tc_commit(&kv_empty[itK % C::NSLOT]);  // both tiles used K_j
-            sj[t] = j + 1;
-            progressed = true;
-          }
-          const int jp = pj[t];
-          const int itV = 2 * jp + 1;
-          if (jp < n && jp < sj[t] && mbar_test(&p_full[t], (uint32_t)jp & 1u) &&
-              mbar_test(&kv_full[itV % C::NSLOT], (uint32_t)(itV / C::NSLOT) & 1u)) {
-            tc_fence_after();
-            const uint32_t vb_addr = sKVa + (itV % C::NSLOT) * C::TILE;
-#pragma unroll
-            for (int k = 0; k < BN / 16; ++k) {  // O_t (+)= P_t V_j
-              const uint64_t bdesc = desc_sw128(vb_addr + k * 2048, C::CHUNK, 1024);
-              const uint32_t acc = (jp > 0 || k > 0) ? 1u : 0u;
-              if constexpr (C::P_SMEM) {
-                const uint32_t poff = t * C::P_TILE + (k >> 2) * C::CHUNK + (k & 3) * 32;
-                mma_ss(tmem + 256u + DP * t, desc_sw128(sPa + poff, 16, 1024), bdesc, kIdPV, acc);
-              } else {
-                mma_ts(tmem + 256u + DP * t, tmem + C::TMEM_P + 64u * t + k * 8, bdesc, kIdPV, acc);
-              }
-            }
-            tc_commit(&pv_done[t]);
-            if (pj[1 - t] > jp) tc_commit(&kv_empty[itV % C::NSLOT]);  // both tiles used V_j
-            pj[t] = jp + 1;
-            progressed = true;
-          }
+        for (int k = 0; k < DP / 16; ++k) {
+          const uint32_t koff = (k >> 2) * C::CHUNK + (k & 3) * 32;
+          mma_ss(tmem + 128u * t, desc_sw128(sQa + t * C::TILE + koff, 16, 1024),
+                 desc_sw128(kb_addr + koff, 16, 1024), kIdQK, k > 0);
         }
-        if (progressed) {
-          idle_polls = 0;
-        } else if (++idle_polls == 1) {
-          idle_since = globaltimer_ns();
-        } else if ((idle_polls & 255u) == 0) {
-          if (*abort_flag || globaltimer_ns() - idle_since > kWaitTimeoutNs) {
-            *abort_flag = 1;
-            ok = false;
-          }
+      };
+      auto pv = [&](int t, int it, bool acc) {  // O_t (+)= P_t V, V in ring item `it`
+        const uint32_t vb_addr = sKVa + (it % C::NSLOT) * C::TILE;
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k)
+          mma_ts(tmem + 256u + DP * t, tmem + 128u * t + k * 8,
+                 desc_sw128(vb_addr + k * 2048, C::CHUNK, 1024), kIdPV, (acc || k > 0) ? 1u : 0u);
+      };
+      auto ring_wait = [&](int it) {
+        return mbar_wait(&kv_full[it % C::NSLOT], (uint32_t)(it / C::NSLOT) & 1u, abort_flag);
+      };
+      bool ok = mbar_wait(&q_full[0], 0, abort_flag) && mbar_wait(&q_full[1], 0, abort_flag) &&
+                ring_wait(0);
+      if (ok) {
+        tc_fence_after();
+        qk(0, 0);
+        tc_commit(&s_full[0]);
+        qk(1, 0);
+        tc_commit(&s_full[1]);
+        tc_commit(&kv_empty[0]);
+      }
+      for (int j = 0; j < n && ok; ++j) {
+        const int itV = 2 * j + 1, itK = 2 * j + 2;
+        const bool more = j + 1 < n;
+        ok = ring_wait(itV) && mbar_wait(&p_full[0], (uint32_t)j & 1u, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        pv(0, itV, j > 0);
+        if (!more) tc_commit(&o_full[0]);
+        if (more) {
+          if (!(ok = ring_wait(itK))) break;
+          tc_fence_after();
+          qk(0, itK);
+          tc_commit(&s_full[0]);
+        }
+        if (!(ok = mbar_wait(&p_full[1], (uint32_t)j & 1u, abort_flag))) break;
+        tc_fence_after();
+        pv(1, itV, j > 0);
+        tc_commit(&kv_empty[itV % C::NSLOT]);
+        if (!more) tc_commit(&o_full[1]);
+        if (more) {
+          qk(1, itK);
+          tc_commit(&s_full[1]);
+          tc_commit(&kv_empty[itK % C::NSLOT]);
         }
       }
       // Drain: every MMA issued above has completed before TMEM is released.
@@ -285,8 +265,6 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
     const uint32_t tS = tmem + lane_base + t * 128;
     const uint32_t tO = tmem + lane_base + 256 + t * DP;
-    const uint32_t tP = tmem + lane_base + C::TMEM_P + t * 64;
-    uint8_t* sProw = sP + t * C::P_TILE + rt * 128;  // this row inside the swizzled P tile
     const KeyRange kr = key_range(a, sv, row);
     // tile-uniform interval extremes for the "block needs no mask" test
     const int tile_lo_max = key_range(a, sv, (int64_t)r0 + t * BM + BM - 1).lo;
@@ -319,10 +297,6 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
       tmem_ld_tie32(r + 32);
       tmem_ld_tie32(r + 64);
       tmem_ld_tie32(r + 96);
-      // S_t is in registers: hand the TMEM columns back for S_t(j+1)
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[t]);
       float x[128];
       const int c0 = (jb + j) * BN;
       const bool need_mask = (c0 < tile_lo_max) || (c0 + BN > tile_hi_min);
@@ -383,15 +357,10 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
       mx1 = fmax3(mx1, x[126], x[127]);
       const float m_new = fmax3(m_used, fmaxf(mx0, mx1), fmaxf(mx2, mx3));
       const bool grow = (m_new - m_used) * c > 8.f;  // false when both are -inf (NaN compare)
-      // P_t and O_t are in use by P_t(j-1) V_{j-1} until pv_done
-      if (j > 0) {
-        ok = __all_sync(kFull, mbar_wait(&pv_done[t], (uint32_t)(j - 1) & 1u, abort_flag));
-        if (!ok) break;
-        tc_fence_after();
-      }
       if (__any_sync(kFull, grow)) {
         const float factor = (m_used == -INFINITY) ? 0.f : ex2((m_used - m_new) * c);
         if (j > 0) {
+          // O_t is idle here: the commit that published S_t(j) also covered PV_t(j-1).
 #pragma unroll 1
           for (int cc = 0; cc < DP; cc += 32) {
             uint32_t o[32];
@@ -432,32 +401,18 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
           f2unpack(p2, p0, p1);
           pk[i] = pack2<kBF16>(p0, p1);
         }
-        if constexpr (C::P_SMEM) {
-          // keys 32cc..32cc+31 = four 16-byte units of the row in 128B-swizzled chunk cc/2
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int u = (4 * cc + q) & 7;
-            uint4* dst = reinterpret_cast<uint4*>(sProw + (cc >> 1) * C::CHUNK + ((u ^ (rt & 7)) << 4));
-            *dst = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          }
-        } else {
-          tmem_st16(tP + 16 * cc, pk);
-        }
+        tmem_st16(tS + 16 * cc, pk);  // P_t over the first 64 columns of S_t
       }
       float la, lb;
       f2unpack(fadd2(acc0, acc1), la, lb);
       l += la + lb;
-      if constexpr (C::P_SMEM) {
-        fence_proxy_async_smem();
-      } else {
-        tmem_st_wait();
-      }
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
     }
     if (ok && n > 0) {
-      ok = __all_sync(kFull, mbar_wait(&pv_done[t], (uint32_t)(n - 1) & 1u, abort_flag));
+      ok = __all_sync(kFull, mbar_wait(&o_full[t], 0, abort_flag));
     }
     if (ok) {
       tc_fence_after();
