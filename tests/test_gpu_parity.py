@@ -49,6 +49,8 @@ def bar_check(out, want, dtype, what):
     assert excess <= BAR[dtype], (f"{what}: error beyond output rounding {excess:.3e} "
                                   f"(max abs {plain:.3e}, oracle's own rounding {ref_round:.3e})")
     return plain, ref_round
+
+
 DEV = "cuda"
 CASES = load_cases()
 
