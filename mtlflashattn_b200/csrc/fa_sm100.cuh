@@ -4,14 +4,17 @@
 // One CTA owns 256 query rows of one (batch, head) as two 128-row tiles (t = 0, 1) and streams
 // the key/value blocks (128 keys each) that any of those rows may attend.
 //
-//   warps 0-3   softmax for tile 0   (TMEM lanes 0-127, one query row per thread)
-//   warps 4-7   softmax for tile 1
-//   warp  8     TMA producer: Q tiles once, then K_j, V_j into a shared ring of NSLOT slots
-//   warp  9     TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 10-11 idle (they complete the third warpgroup, whose registers go to the softmax)
-// Registers: launched at 168 per thread (384 threads); the softmax warpgroups raise theirs to
-// kSoftmaxRegs and the producer/MMA warpgroup lowers its to kOtherRegs (setmaxnreg), so each
-// softmax thread keeps a full 128-column row of S in registers without spilling.
+//   warpgroups 0 .. 2*CG-1   softmax: tile t = wg / CG, key columns [cg*128/CG, (cg+1)*128/CG)
+//                            with cg = wg % CG (TMEM lanes 0-127, one query row per thread)
+//   warp 8*CG                TMA producer: Q tiles once, then K_j, V_j into a ring of NSLOT
+//   warp 8*CG+1              TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 8*CG+2, 8*CG+3     idle (they complete the last warpgroup)
+// With CG = 2 each row's 128 scores are split over two threads in two warpgroups that exchange
+// their partial row maxima (and, at the end, row sums) through shared memory behind a named
+// barrier: twice the softmax warps per SM sub-partition to hide the TMEM / MUFU latencies.
+// Registers: the softmax warpgroups raise theirs and the producer/MMA warpgroup lowers its
+// with setmaxnreg (Roles<CG> below), so each softmax thread keeps its share of a row of S in
+// registers without spilling.
 //
 // TMEM columns (512 allocated): S0 [0,128) S1 [128,256) O0 [256,256+DP) O1 [256+DP,256+2DP).
 // P_t (16-bit, two per column) overwrites the first 64 columns of S_t once S_t is in registers.
@@ -41,12 +44,23 @@ namespace sm100 {
 
 constexpr int BM = 128;  // query rows per tile (TMEM lanes)
 constexpr int BN = 128;  // keys per block
-constexpr int kThreads = 384;
-constexpr int kLaunchRegs = 168;  // 65536 / 384 rounded down to a multiple of 8
-constexpr int kSoftmaxRegs = 208;
-constexpr int kOtherRegs = 88;
-static_assert(2 * 128 * kSoftmaxRegs + 128 * kOtherRegs <= kThreads * kLaunchRegs,
-              "setmaxnreg split exceeds the launch register budget");
+
+// Thread roles and register budget for CG column groups per tile.
+template <int CG>
+struct Roles {
+  static constexpr int kSoftWarps = 8 * CG;
+  static constexpr int kProducer = kSoftWarps;
+  static constexpr int kMma = kSoftWarps + 1;
+  static constexpr int kThreads = 128 * (2 * CG + 1);
+  // registers per thread at launch: the register file of one SM sub-partition (16384) over the
+  // warps it holds, rounded down to a multiple of 8
+  static constexpr int kLaunchRegs = CG == 1 ? 168 : 96;
+  static constexpr int kSoftmaxRegs = CG == 1 ? 208 : 104;
+  static constexpr int kOtherRegs = CG == 1 ? 88 : 64;
+  static constexpr int NC = 128 / CG;  // score columns per softmax thread
+  static_assert(2 * CG * 128 * kSoftmaxRegs + 128 * kOtherRegs <= kThreads * kLaunchRegs,
+                "setmaxnreg split exceeds the launch register budget");
+};
 
 template <int DP>
 struct Cfg {
@@ -55,7 +69,8 @@ struct Cfg {
   static constexpr uint32_t TILE = NCH * CHUNK;          // Q tile or K / V block
   static constexpr int NSLOT = DP == 128 ? 3 : 6;        // K/V ring depth
   static constexpr uint32_t BAR_OFF = 2 * TILE + NSLOT * TILE;
-  static constexpr uint32_t SMEM = BAR_OFF + 256 + 1024;  // + barriers + alignment slack
+  static constexpr uint32_t XCH_OFF = BAR_OFF + 256;  // [parity][tile][cg][row] fp32 exchange
+  static constexpr uint32_t SMEM = XCH_OFF + 4096 + 1024;  // + alignment slack
 };
 
 // Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.
@@ -83,10 +98,26 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 #ifndef MFA_EMU128
 #define MFA_EMU128 0
 #endif
-template <int DP, bool kBF16, bool kGeneral, int kEmu = (DP == 64 ? MFA_EMU64 : MFA_EMU128)>
-__global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_constant__ Sm100Args args) {
+// Column groups per tile; see the role table above. Measured on B200: the softcap / ALiBi path
+// (more work per score) gains 17-29% from CG = 2, the plain path loses 9-17%.
+template <bool kGeneral>
+struct DefaultCG {
+  static constexpr int value = kGeneral ? 2 : 1;
+};
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+template <int DP, bool kBF16, bool kGeneral, int CG = DefaultCG<kGeneral>::value,
+          int kEmu = (DP == 64 ? MFA_EMU64 : MFA_EMU128)>
+__global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
+    fa_fwd_sm100(const __grid_constant__ Sm100Args args) {
   using namespace sm100;
   using C = Cfg<DP>;
+  using R = Roles<CG>;
+  constexpr int kSoftmaxRegs = R::kSoftmaxRegs;
+  constexpr int kOtherRegs = R::kOtherRegs;
+  constexpr int NC = R::NC;
   const FwdArgs& a = args.a;
 
   extern __shared__ uint8_t smem_raw[];
@@ -104,6 +135,7 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
   uint64_t* mma_done = o_full + 2;         // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* xch = reinterpret_cast<float*>(sb + C::XCH_OFF);
 
   // ---- work decode: heaviest row blocks first across all (batch, head)
   const int HB = a.Hq * a.B;
@@ -136,18 +168,18 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 4);
+      mbar_init(&p_full[t], 4 * CG);
       mbar_init(&o_full[t], 1);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == R::kMma) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == R::kProducer && lane == 0) {
     tma_prefetch_map(&args.tq);
     tma_prefetch_map(&args.tk);
     tma_prefetch_map(&args.tv);
@@ -157,9 +189,9 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= 10) {
+  if (warp >= R::kMma + 1) {
     regs_dec<kOtherRegs>();  // idle warps of the producer/MMA warpgroup
-  } else if (warp == 8) {
+  } else if (warp == R::kProducer) {
     regs_dec<kOtherRegs>();
     // ------------------------------------------------------------ TMA producer
     if (n > 0) {
@@ -188,7 +220,7 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
         __syncwarp();
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == R::kMma) {
     // ------------------------------------------------------------ MMA issuer (one thread)
     regs_dec<kOtherRegs>();
     if (n > 0 && lane == 0) {
@@ -258,7 +290,10 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
   } else {
     // ------------------------------------------------------------ softmax warpgroups
     regs_inc<kSoftmaxRegs>();
-    const int t = warp >> 2;        // tile
+    const int wg = warp >> 2;
+    const int t = wg / CG;          // tile
+    const int cg = wg % CG;         // column group within the row
+    const int col0 = cg * NC;       // first score column of this thread
     const int wq = warp & 3;        // TMEM lane quarter
     const int rt = wq * 32 + lane;  // row within tile
     const int64_t row = (int64_t)r0 + t * BM + rt;  // row within the sequence
@@ -280,6 +315,8 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
     const float sc_a = cap * kLog2e, sc_b = -2.f * cap * kLog2e;
     const float pl_scale = a.scale * kLog2e;  // no softcap: x = s*scale*log2e
     const float centre = (float)(row + sv.off);
+    // partner exchange slots: xch[parity][t][cg][row]
+    auto xslot = [&](int parity, int g) { return xch + ((parity * 2 + t) * 2 + g) * 128 + rt; };
 
     float m_used = -INFINITY;  // in x units
     float l = 0.f;
@@ -288,23 +325,20 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
       ok = __all_sync(kFull, mbar_wait(&s_full[t], (uint32_t)j & 1u, abort_flag));
       if (!ok) break;
       tc_fence_after();
-      uint32_t r[128];
-      tmem_ld32(tS + 0, r);
-      tmem_ld32(tS + 32, r + 32);
-      tmem_ld32(tS + 64, r + 64);
-      tmem_ld32(tS + 96, r + 96);
+      uint32_t r[NC];
+#pragma unroll
+      for (int q = 0; q < NC / 32; ++q) tmem_ld32(tS + col0 + 32 * q, r + 32 * q);
       tmem_ld_wait32(r);
-      tmem_ld_tie32(r + 32);
-      tmem_ld_tie32(r + 64);
-      tmem_ld_tie32(r + 96);
-      float x[128];
-      const int c0 = (jb + j) * BN;
-      const bool need_mask = (c0 < tile_lo_max) || (c0 + BN > tile_hi_min);
+#pragma unroll
+      for (int q = 1; q < NC / 32; ++q) tmem_ld_tie32(r + 32 * q);
+      float x[NC];
+      const int c0 = (jb + j) * BN + col0;  // local key index of x[0]
+      const bool need_mask = ((jb + j) * BN < tile_lo_max) || ((jb + j) * BN + BN > tile_hi_min);
       if constexpr (kGeneral) {
         // x = log2(e) * (softcap(s * scale) - slope * |centre - key|)
         const float d0 = centre - (float)(c0 + a.k_pos_offset);  // centre - key for i = 0
 #pragma unroll
-        for (int i = 0; i < 128; i += 2) {
+        for (int i = 0; i < NC; i += 2) {
           uint64_t s2 = f2pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
           uint64_t x2;
           if (cap > 0.f) {
@@ -327,7 +361,7 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
         }
         if (need_mask) {
 #pragma unroll
-          for (int i = 0; i < 128; ++i) {
+          for (int i = 0; i < NC; ++i) {
             const int kl = c0 + i;
             if (kl < kr.lo || kl >= kr.hi) x[i] = -INFINITY;
           }
@@ -335,34 +369,41 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
       } else {
         if (need_mask) {
 #pragma unroll
-          for (int i = 0; i < 128; ++i) {
+          for (int i = 0; i < NC; ++i) {
             const int kl = c0 + i;
             x[i] = (kl < kr.lo || kl >= kr.hi) ? -INFINITY : __uint_as_float(r[i]);
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 128; ++i) x[i] = __uint_as_float(r[i]);
+          for (int i = 0; i < NC; ++i) x[i] = __uint_as_float(r[i]);
         }
       }
       float mx0 = fmax3(x[0], x[1], x[2]), mx1 = fmax3(x[3], x[4], x[5]);
       float mx2 = fmax3(x[6], x[7], x[8]), mx3 = fmax3(x[9], x[10], x[11]);
 #pragma unroll
-      for (int i = 12; i < 124; i += 8) {
+      for (int i = 12; i < NC - 4; i += 8) {
         mx0 = fmax3(mx0, x[i], x[i + 1]);
         mx1 = fmax3(mx1, x[i + 2], x[i + 3]);
         mx2 = fmax3(mx2, x[i + 4], x[i + 5]);
         mx3 = fmax3(mx3, x[i + 6], x[i + 7]);
       }
-      mx0 = fmax3(mx0, x[124], x[125]);
-      mx1 = fmax3(mx1, x[126], x[127]);
-      const float m_new = fmax3(m_used, fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      mx0 = fmax3(mx0, x[NC - 4], x[NC - 3]);
+      mx1 = fmax3(mx1, x[NC - 2], x[NC - 1]);
+      float mrow = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      if constexpr (CG == 2) {
+        // combine with the partner thread that holds the other half of this row
+        *xslot(j & 1, cg) = mrow;
+        named_barrier(1 + t, 256);
+        mrow = fmaxf(mrow, *xslot(j & 1, cg ^ 1));
+      }
+      const float m_new = fmaxf(m_used, mrow);
       const bool grow = (m_new - m_used) * c > 8.f;  // false when both are -inf (NaN compare)
-      if (__any_sync(kFull, grow)) {
+      if (__any_sync(kFull, grow)) {  // same rows in both halves -> same decision
         const float factor = (m_used == -INFINITY) ? 0.f : ex2((m_used - m_new) * c);
         if (j > 0) {
           // O_t is idle here: the commit that published S_t(j) also covered PV_t(j-1).
 #pragma unroll 1
-          for (int cc = 0; cc < DP; cc += 32) {
+          for (int cc = cg * (DP / CG); cc < (cg + 1) * (DP / CG); cc += 32) {
             uint32_t o[32];
             tmem_ld32(tO + cc, o);
             tmem_ld_wait32(o);
@@ -382,7 +423,7 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
       const uint64_t c2 = f2pack(c, c), nref2 = f2pack(-ref, -ref);
       uint64_t acc0 = f2pack(0.f, 0.f), acc1 = acc0;
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {  // 32 keys -> 16 packed words per step
+      for (int cc = 0; cc < NC / 32; ++cc) {  // 32 keys -> 16 packed words per step
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -401,7 +442,7 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
           f2unpack(p2, p0, p1);
           pk[i] = pack2<kBF16>(p0, p1);
         }
-        tmem_st16(tS + 16 * cc, pk);  // P_t over the first 64 columns of S_t
+        tmem_st16(tS + col0 / 2 + 16 * cc, pk);  // P_t over the first 64 columns of S_t
       }
       float la, lb;
       f2unpack(fadd2(acc0, acc1), la, lb);
@@ -414,6 +455,12 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
     if (ok && n > 0) {
       ok = __all_sync(kFull, mbar_wait(&o_full[t], 0, abort_flag));
     }
+    if constexpr (CG == 2) {
+      // row sum = both halves (both threads of a row agree on ok: same barrier waits)
+      *xslot(n & 1, cg) = l;
+      named_barrier(1 + t, 256);
+      l += *xslot(n & 1, cg ^ 1);
+    }
     if (ok) {
       tc_fence_after();
       const bool store = row < sv.lq;
@@ -425,7 +472,7 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
                esz * ((int64_t)sv.qb * a.o_sb + (int64_t)(sv.q0 + row) * a.o_ss + (int64_t)h * a.o_sh);
       }
 #pragma unroll 1
-      for (int cc = 0; cc < DP; cc += 32) {
+      for (int cc = cg * (DP / CG); cc < (cg + 1) * (DP / CG); cc += 32) {
         float vals[32];
         if (n > 0) {
           uint32_t o[32];
@@ -440,7 +487,7 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
         const int nc = min(32, a.D - cc);
         if (store && nc > 0) store_row_chunk(a, orow, cc, vals, nc);
       }
-      if (store && a.lse != nullptr) {
+      if (store && cg == 0 && a.lse != nullptr) {
         const float lse = l > 0.f ? (m_used * c + __log2f(l)) * 0.6931471805599453f : -INFINITY;
         a.lse[(int64_t)sv.qb * a.lse_sb + (int64_t)h * a.lse_sh + sv.q0 + row] = lse;
       }
@@ -450,7 +497,7 @@ __global__ void __launch_bounds__(sm100::kThreads, 1) fa_fwd_sm100(const __grid_
   // ---- teardown
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == R::kMma) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

@@ -214,9 +214,10 @@ int launch_sm100(const Sm100Args& args, int dev, int64_t grid, cudaStream_t st) 
     if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) return MFA_ERR_CUDA;
     launch_regs = fa.numRegs;
   }
-  if (launch_regs != sm100::kLaunchRegs) return MFA_ERR_UNSUPPORTED;
+  constexpr int CG = DefaultCG<GEN>::value;
+  if (launch_regs != sm100::Roles<CG>::kLaunchRegs) return MFA_ERR_UNSUPPORTED;
   if (ensure_smem(k, dev, smem) != cudaSuccess) return MFA_ERR_CUDA;
-  k<<<(unsigned)grid, sm100::kThreads, smem, st>>>(args);
+  k<<<(unsigned)grid, sm100::Roles<CG>::kThreads, smem, st>>>(args);
   return MFA_OK;
 }
 
