@@ -69,7 +69,11 @@ struct Cfg {
   static constexpr uint32_t TILE = NCH * CHUNK;          // Q tile or K / V block
   static constexpr int NSLOT = DP == 128 ? 3 : 6;        // K/V ring depth
   static constexpr uint32_t BAR_OFF = 2 * TILE + NSLOT * TILE;
-  static constexpr uint32_t XCH_OFF = BAR_OFF + 256;  // [parity][tile][cg][row] fp32 exchange
+  static constexpr uint32_t XCH_OFF = BAR_OFF + 256;
+  // D = 64 leaves TMEM columns [384, 512) free: P gets its own columns and S is released to the
+  // MMA as soon as it is in registers (see "decoupled" below). D = 128 aliases P over S.
+  static constexpr bool DECOUPLED = DP == 64;
+  static constexpr uint32_t TMEM_P = 384;  // [parity][tile][cg][row] fp32 exchange
   static constexpr uint32_t SMEM = XCH_OFF + 4096 + 1024;  // + alignment slack
 };
 
@@ -100,9 +104,12 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 #endif
 // Column groups per tile; see the role table above. Measured on B200: the softcap / ALiBi path
 // (more work per score) gains 17-29% from CG = 2, the plain path loses 9-17%.
+#ifndef MFA_CG_PLAIN
+#define MFA_CG_PLAIN 1
+#endif
 template <bool kGeneral>
 struct DefaultCG {
-  static constexpr int value = kGeneral ? 2 : 1;
+  static constexpr int value = kGeneral ? 2 : MFA_CG_PLAIN;
 };
 __device__ __forceinline__ void named_barrier(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
@@ -132,7 +139,9 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
   uint64_t* s_full = kv_empty + C::NSLOT;  // [2]
   uint64_t* p_full = s_full + 2;           // [2]
   uint64_t* o_full = p_full + 2;           // [2]
-  uint64_t* mma_done = o_full + 2;         // [1]
+  uint64_t* s_free = o_full + 2;           // [2] decoupled only
+  uint64_t* pv_done = s_free + 2;          // [2] decoupled only
+  uint64_t* mma_done = pv_done + 2;        // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* xch = reinterpret_cast<float*>(sb + C::XCH_OFF);
@@ -170,6 +179,8 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
       mbar_init(&s_full[t], 1);
       mbar_init(&p_full[t], 4 * CG);
       mbar_init(&o_full[t], 1);
+      mbar_init(&s_free[t], 4 * CG);
+      mbar_init(&pv_done[t], 1);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -228,21 +239,29 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
       constexpr uint32_t kIdPV = idesc_f16(kBF16, BM, DP, true);
       const uint32_t sQa = smem_u32(sQ);
       const uint32_t sKVa = smem_u32(sKV);
+      // Descriptors are built once; each MMA only adds a compile-time offset to the 14-bit
+      // start-address field (shared-memory addresses < 256 KB never carry out of it). Building
+      // them per MMA made the single issuing thread, not the tensor pipe, the bottleneck.
+      const uint64_t dQ = desc_sw128(sQa, 16, 1024);
+      const uint64_t dK = desc_sw128(sKVa, 16, 1024);
+      const uint64_t dV = desc_sw128(sKVa, C::CHUNK, 1024);
       auto qk = [&](int t, int it) {  // S_t = Q_t K^T, K in ring item `it`
-        const uint32_t kb_addr = sKVa + (it % C::NSLOT) * C::TILE;
+        const uint64_t a0 = dQ + ((t * C::TILE) >> 4);
+        const uint64_t b0 = dK + (((it % C::NSLOT) * C::TILE) >> 4);
+        const uint32_t d = tmem + 128u * t;
 #pragma unroll
         for (int k = 0; k < DP / 16; ++k) {
-          const uint32_t koff = (k >> 2) * C::CHUNK + (k & 3) * 32;
-          mma_ss(tmem + 128u * t, desc_sw128(sQa + t * C::TILE + koff, 16, 1024),
-                 desc_sw128(kb_addr + koff, 16, 1024), kIdQK, k > 0);
+          const uint32_t koff = ((k >> 2) * C::CHUNK + (k & 3) * 32) >> 4;
+          mma_ss(d, a0 + koff, b0 + koff, kIdQK, k > 0);
         }
       };
       auto pv = [&](int t, int it, bool acc) {  // O_t (+)= P_t V, V in ring item `it`
-        const uint32_t vb_addr = sKVa + (it % C::NSLOT) * C::TILE;
+        const uint64_t b0 = dV + (((it % C::NSLOT) * C::TILE) >> 4);
+        const uint32_t d = tmem + 256u + DP * t;
+        const uint32_t pa = tmem + (C::DECOUPLED ? C::TMEM_P + 64u * t : 128u * t);
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k)
-          mma_ts(tmem + 256u + DP * t, tmem + 128u * t + k * 8,
-                 desc_sw128(vb_addr + k * 2048, C::CHUNK, 1024), kIdPV, (acc || k > 0) ? 1u : 0u);
+          mma_ts(d, pa + k * 8, b0 + ((k * 2048) >> 4), kIdPV, (acc || k > 0) ? 1u : 0u);
       };
       auto ring_wait = [&](int it) {
         return mbar_wait(&kv_full[it % C::NSLOT], (uint32_t)(it / C::NSLOT) & 1u, abort_flag);
@@ -257,6 +276,36 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
         tc_commit(&s_full[1]);
         tc_commit(&kv_empty[0]);
       }
+      if constexpr (C::DECOUPLED) {
+        // Per block j: S0(j+1) and S1(j+1) as soon as each softmax has S_t(j) in registers,
+        // then P0(j) V_j and P1(j) V_j as each P arrives; pv_done[t] tells the softmax when
+        // O_t and P_t are free again.
+        for (int j = 0; j < n && ok; ++j) {
+          const int itV = 2 * j + 1, itK = 2 * j + 2;
+          if (j + 1 < n) {
+            ok = ring_wait(itK) && mbar_wait(&s_free[0], (uint32_t)j & 1u, abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+            qk(0, itK);
+            tc_commit(&s_full[0]);
+            if (!(ok = mbar_wait(&s_free[1], (uint32_t)j & 1u, abort_flag))) break;
+            tc_fence_after();
+            qk(1, itK);
+            tc_commit(&s_full[1]);
+            tc_commit(&kv_empty[itK % C::NSLOT]);
+          }
+          ok = ring_wait(itV) && mbar_wait(&p_full[0], (uint32_t)j & 1u, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          pv(0, itV, j > 0);
+          tc_commit(&pv_done[0]);
+          if (!(ok = mbar_wait(&p_full[1], (uint32_t)j & 1u, abort_flag))) break;
+          tc_fence_after();
+          pv(1, itV, j > 0);
+          tc_commit(&pv_done[1]);
+          tc_commit(&kv_empty[itV % C::NSLOT]);
+        }
+      } else {
       for (int j = 0; j < n && ok; ++j) {
         const int itV = 2 * j + 1, itK = 2 * j + 2;
         const bool more = j + 1 < n;
@@ -281,6 +330,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
           tc_commit(&s_full[1]);
           tc_commit(&kv_empty[itK % C::NSLOT]);
         }
+      }
       }
       // Drain: every MMA issued above has completed before TMEM is released.
       tc_commit(mma_done);
@@ -331,6 +381,11 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
       tmem_ld_wait32(r);
 #pragma unroll
       for (int q = 1; q < NC / 32; ++q) tmem_ld_tie32(r + 32 * q);
+      if constexpr (C::DECOUPLED) {  // S_t is in registers: the MMA may write S_t(j+1)
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[t]);
+      }
       float x[NC];
       const int c0 = (jb + j) * BN + col0;  // local key index of x[0]
       const bool need_mask = ((jb + j) * BN < tile_lo_max) || ((jb + j) * BN + BN > tile_hi_min);
@@ -396,12 +451,20 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
         named_barrier(1 + t, 256);
         mrow = fmaxf(mrow, *xslot(j & 1, cg ^ 1));
       }
+      if constexpr (C::DECOUPLED) {  // O_t and P_t stay busy until P_t(j-1) V_{j-1} is done
+        if (j > 0) {
+          ok = __all_sync(kFull, mbar_wait(&pv_done[t], (uint32_t)(j - 1) & 1u, abort_flag));
+          if (!ok) break;
+          tc_fence_after();
+        }
+      }
       const float m_new = fmaxf(m_used, mrow);
       const bool grow = (m_new - m_used) * c > 8.f;  // false when both are -inf (NaN compare)
       if (__any_sync(kFull, grow)) {  // same rows in both halves -> same decision
         const float factor = (m_used == -INFINITY) ? 0.f : ex2((m_used - m_new) * c);
         if (j > 0) {
-          // O_t is idle here: the commit that published S_t(j) also covered PV_t(j-1).
+          // O_t is idle here: decoupled, after pv_done; aliased, because the commit that
+          // published S_t(j) also covered PV_t(j-1).
 #pragma unroll 1
           for (int cc = cg * (DP / CG); cc < (cg + 1) * (DP / CG); cc += 32) {
             uint32_t o[32];
@@ -442,7 +505,8 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
           f2unpack(p2, p0, p1);
           pk[i] = pack2<kBF16>(p0, p1);
         }
-        tmem_st16(tS + col0 / 2 + 16 * cc, pk);  // P_t over the first 64 columns of S_t
+        // P_t: its own columns (decoupled) or over the first 64 columns of S_t
+        tmem_st16((C::DECOUPLED ? tmem + lane_base + C::TMEM_P + t * 64 : tS) + col0 / 2 + 16 * cc, pk);
       }
       float la, lb;
       f2unpack(fadd2(acc0, acc1), la, lb);
@@ -453,7 +517,9 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
       if (lane == 0) mbar_arrive(&p_full[t]);
     }
     if (ok && n > 0) {
-      ok = __all_sync(kFull, mbar_wait(&o_full[t], 0, abort_flag));
+      ok = __all_sync(kFull, C::DECOUPLED
+                                 ? mbar_wait(&pv_done[t], (uint32_t)(n - 1) & 1u, abort_flag)
+                                 : mbar_wait(&o_full[t], 0, abort_flag));
     }
     if constexpr (CG == 2) {
       // row sum = both halves (both threads of a row agree on ok: same barrier waits)
