@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define MFA_ABI_VERSION 1
+#define MFA_ABI_VERSION 2
 
 /* Status codes. The Python layer maps them to the reference's exception types. */
 enum mfa_status {
@@ -84,6 +84,11 @@ typedef struct mfa_fwd_params {
   int32_t lk_total;
   int32_t kernel;      /* mfa_kernel */
   int32_t* err;        /* optional device int; a kernel that times out stores MFA_ERR_TIMEOUT */
+  /* Optional caller-owned device scratch for splitting the keys of one launch over several
+   * CTAs when there are too few query rows to fill the GPU (decode-like Lq). Size it with
+   * mfa_fwd_workspace_size; NULL or too small simply disables the split. */
+  void* workspace;
+  size_t workspace_bytes;
 } mfa_fwd_params;
 
 /* Attention forward. Replaces the tier dispatch under flash_attn_forward
@@ -91,6 +96,14 @@ typedef struct mfa_fwd_params {
  * (_kernel.py:1288-1420). Returns MFA_OK or an error; a launch error is reported here,
  * a kernel-side timeout through p->err. */
 int mfa_fwd(const mfa_fwd_params* p, void* cuda_stream);
+
+/* Bytes of workspace mfa_fwd can use for these params on the current device (0 when it would
+ * not split the keys). No counterpart in the reference, whose tiers never split keys. */
+size_t mfa_fwd_workspace_size(const mfa_fwd_params* p);
+
+/* Number of key splits mfa_fwd would use for these params with the workspace they carry (1 =
+ * no split), or a negative mfa_status. Lets callers and tests see the plan. */
+int mfa_fwd_num_splits(const mfa_fwd_params* p);
 
 /* Which kernel mfa_fwd would run for these params (mfa_kernel value, never AUTO), or a
  * negative mfa_status if the call would be rejected. Replaces the label logic of the

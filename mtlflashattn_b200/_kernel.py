@@ -186,7 +186,13 @@ def _run(p, q, what, causal, trace_shape):
             sel = _lib.select_kernel(p)
             label = "cuda/" + _lib.KERNEL_NAMES.get(sel, "rejected")
             _record_trace(q.dtype, trace_shape[0], trace_shape[1], trace_shape[2], causal, label)
+        ws = None
+        need = _lib.workspace_size(p)
+        if need > 0:  # few query rows: let the library split the keys over more CTAs
+            ws = torch.empty(need, dtype=torch.uint8, device=q.device)
+            p.workspace, p.workspace_bytes = ws.data_ptr(), need
         rc = _lib.fwd(p, torch.cuda.current_stream(q.device).cuda_stream)
+        del ws  # the caching allocator keeps it alive for work already queued on this stream
         if rc != _lib.OK:
             if rc == _lib.ERR_UNSUPPORTED and p.kernel != _lib.KERNEL_AUTO:
                 raise RuntimeError(

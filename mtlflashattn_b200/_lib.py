@@ -13,7 +13,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmfa.so")
 
-MFA_ABI_VERSION = 1
+MFA_ABI_VERSION = 2
 
 # mfa_status
 OK = 0
@@ -34,6 +34,8 @@ KERNEL_NAMES = {KERNEL_TCGEN05: "tcgen05", KERNEL_SIMT: "simt"}
 # Every symbol include/mfa.h declares.
 EXPORTED_SYMBOLS = (
     "mfa_fwd",
+    "mfa_fwd_workspace_size",
+    "mfa_fwd_num_splits",
     "mfa_select_kernel",
     "mfa_lse_combine",
     "mfa_status_string",
@@ -77,6 +79,8 @@ class MfaFwdParams(ctypes.Structure):
         ("lk_total", ctypes.c_int32),
         ("kernel", ctypes.c_int32),
         ("err", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
     ]
 
 
@@ -109,6 +113,10 @@ def load(path: str | None = None) -> ctypes.CDLL:
         lib = ctypes.CDLL(p)
         lib.mfa_fwd.argtypes = [ctypes.POINTER(MfaFwdParams), ctypes.c_void_p]
         lib.mfa_fwd.restype = ctypes.c_int
+        lib.mfa_fwd_workspace_size.argtypes = [ctypes.POINTER(MfaFwdParams)]
+        lib.mfa_fwd_workspace_size.restype = ctypes.c_size_t
+        lib.mfa_fwd_num_splits.argtypes = [ctypes.POINTER(MfaFwdParams)]
+        lib.mfa_fwd_num_splits.restype = ctypes.c_int
         lib.mfa_select_kernel.argtypes = [ctypes.POINTER(MfaFwdParams)]
         lib.mfa_select_kernel.restype = ctypes.c_int
         lib.mfa_lse_combine.argtypes = [
@@ -138,6 +146,14 @@ def status_string(status: int) -> str:
 
 def fwd(params: MfaFwdParams, stream: int) -> int:
     return load().mfa_fwd(ctypes.byref(params), ctypes.c_void_p(stream))
+
+
+def workspace_size(params: MfaFwdParams) -> int:
+    return load().mfa_fwd_workspace_size(ctypes.byref(params))
+
+
+def num_splits(params: MfaFwdParams) -> int:
+    return load().mfa_fwd_num_splits(ctypes.byref(params))
 
 
 def select_kernel(params: MfaFwdParams) -> int:

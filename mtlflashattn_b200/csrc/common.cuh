@@ -33,6 +33,13 @@ struct FwdArgs {
   int lk_total;  // 0 = per-sequence Lk
   int* err;
   int num_row_blocks;  // row blocks per (batch, head) for this launch's kernel
+  // key split within one launch (1 = none): CTA (row block, batch, head, split) covers the local
+  // keys [split * split_keys, (split + 1) * split_keys) and writes its partial output at
+  // o + split * o_split_stride and its row log-sum-exp at lse + split * lse_split_stride
+  int num_splits;
+  int split_keys;
+  int64_t o_split_stride;
+  int64_t lse_split_stride;
 };
 
 // One (batch, sequence) view after resolving dense vs varlen.

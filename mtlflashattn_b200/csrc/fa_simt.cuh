@@ -193,4 +193,44 @@ __global__ void lse_combine_kernel(const __grid_constant__ PartPtrs pp, int n, i
   if (lane == 0 && lse_out != nullptr) lse_out[li] = lse;
 }
 
+// Merge of the key splits of one launch (dense layout): partial outputs ws_o fp32
+// [split][B][Lq][Hq][D] normalised by their own sums, row log-sum-exp ws_lse [split][B][Hq][Lq].
+// One warp per (batch, head, row); writes the final row in the caller's dtype and strides.
+template <typename TO>
+__global__ void split_combine_kernel(const FwdArgs a, const float* __restrict__ ws_o,
+                                     const float* __restrict__ ws_lse, TO* o, float* lse_out) {
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = (int64_t)a.B * a.Hq * a.Lq;
+  if (w >= rows) return;
+  const int row = (int)(w % a.Lq);
+  const int bh = (int)(w / a.Lq);
+  const int h = bh % a.Hq, b = bh / a.Hq;
+  const int64_t li = ((int64_t)b * a.Hq + h) * a.Lq + row;
+  const int64_t lstride = (int64_t)a.B * a.Hq * a.Lq;
+  const int64_t ostride = lstride * a.D;
+  const int64_t oi = (((int64_t)b * a.Lq + row) * a.Hq + h) * a.D;
+  float mx = -INFINITY;
+  for (int s = 0; s < a.num_splits; ++s) mx = fmaxf(mx, ws_lse[s * lstride + li]);
+  float tot = 0.f;
+  if (mx != -INFINITY)
+    for (int s = 0; s < a.num_splits; ++s) tot += expf(ws_lse[s * lstride + li] - mx);
+  const float lse = mx == -INFINITY ? -INFINITY : mx + logf(tot);
+  TO* orow = o + (int64_t)b * a.o_sb + (int64_t)row * a.o_ss + (int64_t)h * a.o_sh;
+  for (int d = lane; d < a.D; d += 32) {
+    float acc = 0.f;
+    if (lse != -INFINITY)
+      for (int s = 0; s < a.num_splits; ++s) {
+        const float ls = ws_lse[s * lstride + li];
+        if (ls != -INFINITY) acc = fmaf(expf(ls - lse), ws_o[s * ostride + oi + d], acc);
+      }
+    if constexpr (sizeof(TO) == 4) {
+      orow[d] = acc;
+    } else {
+      orow[d] = TO(acc);
+    }
+  }
+  if (lane == 0 && lse_out != nullptr) lse_out[(int64_t)b * a.lse_sb + (int64_t)h * a.lse_sh + row] = lse;
+}
+
 }  // namespace mfa

@@ -147,10 +147,11 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
   float* xch = reinterpret_cast<float*>(sb + C::XCH_OFF);
 
   // ---- work decode: heaviest row blocks first across all (batch, head)
-  const int HB = a.Hq * a.B;
+  const int HBS = a.Hq * a.B * a.num_splits;
   const int idx = blockIdx.x;
-  const int rb = a.num_row_blocks - 1 - idx / HB;
-  const int hb = idx % HB;
+  const int rb = a.num_row_blocks - 1 - idx / HBS;
+  const int split = (idx % HBS) % a.num_splits;  // splits of one row block run side by side
+  const int hb = (idx % HBS) / a.num_splits;
   const int h = hb % a.Hq;
   const int b = hb / a.Hq;
   const int hk = h / a.group;
@@ -160,8 +161,12 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
 
   const int r_last = min(r0 + 2 * BM, sv.lq) - 1;
   // union of the rows' key intervals: lo and hi are nondecreasing in the row
-  const int klo = key_range(a, sv, r0).lo;
-  const int khi = key_range(a, sv, r_last).hi;
+  int klo = key_range(a, sv, r0).lo;
+  int khi = key_range(a, sv, r_last).hi;
+  if (a.num_splits > 1) {
+    klo = max(klo, split * a.split_keys);
+    khi = min(khi, (split + 1) * a.split_keys);
+  }
   const int jb = klo / BN;
   const int n = khi > klo ? (khi + BN - 1) / BN - jb : 0;
 
@@ -535,7 +540,8 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
       if (store) {
         const int64_t esz = a.o_dtype == 2 ? 4 : 2;
         orow = reinterpret_cast<uint8_t*>(a.o) +
-               esz * ((int64_t)sv.qb * a.o_sb + (int64_t)(sv.q0 + row) * a.o_ss + (int64_t)h * a.o_sh);
+               esz * ((int64_t)split * a.o_split_stride + (int64_t)sv.qb * a.o_sb +
+                      (int64_t)(sv.q0 + row) * a.o_ss + (int64_t)h * a.o_sh);
       }
 #pragma unroll 1
       for (int cc = cg * (DP / CG); cc < (cg + 1) * (DP / CG); cc += 32) {
@@ -555,7 +561,8 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
       }
       if (store && cg == 0 && a.lse != nullptr) {
         const float lse = l > 0.f ? (m_used * c + __log2f(l)) * 0.6931471805599453f : -INFINITY;
-        a.lse[(int64_t)sv.qb * a.lse_sb + (int64_t)h * a.lse_sh + sv.q0 + row] = lse;
+        a.lse[(int64_t)split * a.lse_split_stride + (int64_t)sv.qb * a.lse_sb +
+              (int64_t)h * a.lse_sh + sv.q0 + row] = lse;
       }
     }
   }

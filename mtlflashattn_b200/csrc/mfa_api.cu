@@ -146,7 +146,38 @@ FwdArgs resolve(const mfa_fwd_params* p) {
   a.k_pos_offset = p->k_pos_offset;
   a.lk_total = p->lk_total;
   a.err = p->err;
+  a.num_splits = 1;
   return a;
+}
+
+// ---- key split within one launch (decode-like shapes)
+// When the (row block, batch, head) CTAs of a dense launch cover well under two waves of the
+// GPU and there are enough keys, each CTA's keys are cut into `splits` ranges run by separate
+// CTAs; their partial rows are merged by split_combine_kernel. Ranges are whole 128-key blocks
+// and each holds at least two blocks.
+struct SplitPlan {
+  int splits = 1;
+  int split_keys = 0;
+  size_t bytes = 0;
+};
+SplitPlan plan_splits(const mfa_fwd_params* p, int sms) {
+  SplitPlan sp;
+  if (p->cu_q != nullptr || p->B == 0 || p->Lq == 0 || p->Lk == 0) return sp;
+  const int64_t row_blocks = (p->Lq + 255) / 256;
+  const int64_t ctas = row_blocks * p->Hq * p->B;
+  const int64_t key_blocks = (p->Lk + 127) / 128;
+  if (ctas >= sms || key_blocks < 4) return sp;
+  int64_t s = (2 * (int64_t)sms + ctas - 1) / ctas;
+  s = s < key_blocks / 2 ? s : key_blocks / 2;
+  s = s < 64 ? s : 64;
+  if (s < 2) return sp;
+  const int64_t blocks_per = (key_blocks + s - 1) / s;
+  sp.split_keys = (int)(blocks_per * 128);
+  sp.splits = (int)((p->Lk + sp.split_keys - 1) / sp.split_keys);
+  if (sp.splits < 2) return SplitPlan{};
+  const size_t rows = (size_t)p->B * p->Hq * p->Lq;
+  sp.bytes = (size_t)sp.splits * rows * ((size_t)p->D + 1) * sizeof(float) + 256;
+  return sp;
 }
 
 // tcgen05 path eligibility: 16-bit inputs, D a multiple of 8 (TMA needs 16-byte strides),
@@ -221,7 +252,21 @@ int launch_sm100(const Sm100Args& args, int dev, int64_t grid, cudaStream_t st) 
   return MFA_OK;
 }
 
-int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st) {
+int launch_combine(const FwdArgs& fin, const float* ws_o, const float* ws_lse, void* o,
+                   float* lse, cudaStream_t st) {
+  const int64_t warps = (int64_t)fin.B * fin.Hq * fin.Lq;
+  const unsigned blocks = (unsigned)((warps * 32 + 255) / 256);
+  if (fin.o_dtype == MFA_FP32)
+    split_combine_kernel<float><<<blocks, 256, 0, st>>>(fin, ws_o, ws_lse, (float*)o, lse);
+  else if (fin.o_dtype == MFA_BF16)
+    split_combine_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(fin, ws_o, ws_lse, (__nv_bfloat16*)o, lse);
+  else
+    split_combine_kernel<__half><<<blocks, 256, 0, st>>>(fin, ws_o, ws_lse, (__half*)o, lse);
+  return MFA_OK;
+}
+
+int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
+              const SplitPlan& split, void* workspace) {
   Sm100Args args;
   std::memset(&args, 0, sizeof(args));
   const bool varlen = p->cu_q != nullptr;
@@ -233,14 +278,43 @@ int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st) {
   if ((rc = make_map(&args.tk, p->k, p->dtype, p->D, p->Hkv, Sk, Bm, p->k_stride)) != MFA_OK) return rc;
   if ((rc = make_map(&args.tv, p->v, p->dtype, p->D, p->Hkv, Sk, Bm, p->v_stride)) != MFA_OK) return rc;
   a.num_row_blocks = (a.max_lq + 2 * sm100::BM - 1) / (2 * sm100::BM);
+  FwdArgs fin = a;  // the caller's output, for the split merge
+  fin.num_splits = split.splits;
+  float* ws_o = nullptr;
+  float* ws_lse = nullptr;
+  if (split.splits > 1) {
+    // partials: fp32 [split][B][Lq][Hq][D] and row lse [split][B][Hq][Lq] in the workspace
+    uintptr_t base = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~(uintptr_t)255;
+    ws_o = reinterpret_cast<float*>(base);
+    const int64_t rows = (int64_t)p->B * p->Hq * p->Lq;
+    ws_lse = ws_o + (int64_t)split.splits * rows * p->D;
+    a.o = ws_o;
+    a.o_dtype = MFA_FP32;
+    a.o_sb = (int64_t)p->Lq * p->Hq * p->D;
+    a.o_ss = (int64_t)p->Hq * p->D;
+    a.o_sh = p->D;
+    a.o_vec16 = 0;
+    a.lse = ws_lse;
+    a.lse_sb = (int64_t)p->Hq * p->Lq;
+    a.lse_sh = p->Lq;
+    a.num_splits = split.splits;
+    a.split_keys = split.split_keys;
+    a.o_split_stride = rows * p->D;
+    a.lse_split_stride = rows;
+  }
   args.a = a;
-  const int64_t grid = (int64_t)a.num_row_blocks * a.Hq * a.B;
+  const int64_t grid = (int64_t)a.num_row_blocks * a.Hq * a.B * a.num_splits;
   if (grid == 0) return MFA_OK;
   if (grid >= (1ll << 31)) return MFA_ERR_UNSUPPORTED;
   const bool gen = !(a.scale > 0.f) || a.softcap > 0.f || a.alibi != nullptr;
   const bool bf = p->dtype == MFA_BF16;
   const bool wide = p->D > 64;
-#define MFA_SM100(DP, BF, G) return launch_sm100<DP, BF, G>(args, dev, grid, st)
+#define MFA_SM100(DP, BF, G)                                                     \
+  do {                                                                           \
+    const int rc_ = launch_sm100<DP, BF, G>(args, dev, grid, st);                \
+    if (rc_ != MFA_OK || split.splits < 2) return rc_;                           \
+    return launch_combine(fin, ws_o, ws_lse, p->o, p->lse, st);                  \
+  } while (0)
   if (wide) {
     if (bf) { if (gen) MFA_SM100(128, true, true); MFA_SM100(128, true, false); }
     if (gen) MFA_SM100(128, false, true);
@@ -296,6 +370,24 @@ const char* mfa_status_string(int s) {
   }
 }
 
+size_t mfa_fwd_workspace_size(const mfa_fwd_params* p) {
+  if (mfa::validate(p) != MFA_OK) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (mfa::pick_kernel(p, dev) != MFA_KERNEL_TCGEN05) return 0;
+  return mfa::plan_splits(p, mfa::dev_info(dev).sms).bytes;
+}
+
+int mfa_fwd_num_splits(const mfa_fwd_params* p) {
+  int rc = mfa::validate(p);
+  if (rc != MFA_OK) return -rc;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -MFA_ERR_NO_DEVICE;
+  if (mfa::pick_kernel(p, dev) != MFA_KERNEL_TCGEN05 || p->workspace == nullptr) return 1;
+  const mfa::SplitPlan sp = mfa::plan_splits(p, mfa::dev_info(dev).sms);
+  return (sp.splits > 1 && p->workspace_bytes >= sp.bytes) ? sp.splits : 1;
+}
+
 int mfa_select_kernel(const mfa_fwd_params* p) {
   int rc = mfa::validate(p);
   if (rc != MFA_OK) return -rc;
@@ -317,7 +409,13 @@ int mfa_fwd(const mfa_fwd_params* p, void* stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   (void)cudaGetLastError();
   mfa::FwdArgs a = mfa::resolve(p);
-  rc = kern == MFA_KERNEL_TCGEN05 ? mfa::run_sm100(p, a, dev, st) : mfa::run_simt(p, a, st);
+  mfa::SplitPlan split;
+  if (kern == MFA_KERNEL_TCGEN05 && p->workspace != nullptr) {
+    split = mfa::plan_splits(p, mfa::dev_info(dev).sms);
+    if (split.splits > 1 && p->workspace_bytes < split.bytes) split = mfa::SplitPlan{};
+  }
+  rc = kern == MFA_KERNEL_TCGEN05 ? mfa::run_sm100(p, a, dev, st, split, p->workspace)
+                                  : mfa::run_simt(p, a, st);
   if (rc != MFA_OK) return rc;
   return cudaGetLastError() == cudaSuccess ? MFA_OK : MFA_ERR_CUDA;
 }

@@ -222,7 +222,8 @@ def test_varlen_single_sequence_matches_dense():
     qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
     out_v = mfa.flash_attn_varlen_func(qd, kd, vd, cu_q.to(DEV), cu_k.to(DEV), 777, 777, causal=True)
     out_d = mfa.flash_attn_func(qd[None], kd[None], vd[None], causal=True)[0]
-    torch.testing.assert_close(out_v, out_d, atol=0, rtol=0)
+    # the dense call may split its keys over more CTAs (few rows), so compare within tolerance
+    torch.testing.assert_close(out_v.float(), out_d.float(), **TOL[torch.bfloat16])
 
 
 def test_varlen_ragged_with_empty_sequences():
