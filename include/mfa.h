@@ -43,7 +43,8 @@ enum mfa_status {
   MFA_ERR_CUDA = 3,           /* CUDA runtime / driver failure (RuntimeError) */
   MFA_ERR_TIMEOUT = 4,        /* a bounded in-kernel wait expired; output is invalid */
   MFA_ERR_NO_DEVICE = 5,      /* no usable sm_100 device for the requested kernel */
-  MFA_ERR_FAULT_INJECTED = 6  /* host-side fault injection (MFA_FAULT env) fired */
+  MFA_ERR_FAULT_INJECTED = 6, /* host-side fault injection (MFA_FAULT env) fired */
+  MFA_ERR_SCRATCH_TOO_SMALL = 7 /* mfa_fwd_noalloc: the problem needs more than its scratch */
 };
 
 enum mfa_dtype { MFA_FP16 = 0, MFA_BF16 = 1, MFA_FP32 = 2 };
@@ -96,6 +97,22 @@ typedef struct mfa_fwd_params {
  * (_kernel.py:1288-1420). Returns MFA_OK or an error; a launch error is reported here,
  * a kernel-side timeout through p->err. */
 int mfa_fwd(const mfa_fwd_params* p, void* cuda_stream);
+
+/* mfa_fwd for callers that cannot allocate device memory (no counterpart in the reference).
+ * Some callers cannot call cudaMalloc during a forward: code running under an allocator that
+ * owns all device memory, a custom memory pool, or a real-time loop that must not take the
+ * allocator's locks or trigger an implicit synchronisation. This entry point takes the same
+ * params (their workspace fields are ignored) and allocates nothing: when the keys are split
+ * over extra CTAs, the partial results go to a fixed 16 MiB device array inside the library,
+ * which every GPU that loads libmfa.so holds until the process exits. A problem that would
+ * need more than 16 MiB of that scratch is rejected with MFA_ERR_SCRATCH_TOO_SMALL (use
+ * mfa_fwd with a workspace for it); problems that do not split need no scratch at all.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
+ * that device current; make that first call before any stream capture. All calls share the
+ * one array: calls whose kernels can overlap on the GPU (different streams, or several host
+ * threads) race on it and must be serialised by the caller. Nothing in it needs to start at
+ * zero: each call overwrites every slot it reads. */
+int mfa_fwd_noalloc(const mfa_fwd_params* p, void* cuda_stream);
 
 /* Bytes of workspace mfa_fwd can use for these params on the current device (0 when it would
  * not split the keys). No counterpart in the reference, whose tiers never split keys. */

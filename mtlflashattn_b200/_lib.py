@@ -23,6 +23,7 @@ ERR_CUDA = 3
 ERR_TIMEOUT = 4
 ERR_NO_DEVICE = 5
 ERR_FAULT_INJECTED = 6
+ERR_SCRATCH_TOO_SMALL = 7
 
 # mfa_dtype
 FP16, BF16, FP32 = 0, 1, 2
@@ -34,6 +35,7 @@ KERNEL_NAMES = {KERNEL_TCGEN05: "tcgen05", KERNEL_SIMT: "simt"}
 # Every symbol include/mfa.h declares.
 EXPORTED_SYMBOLS = (
     "mfa_fwd",
+    "mfa_fwd_noalloc",
     "mfa_fwd_workspace_size",
     "mfa_fwd_num_splits",
     "mfa_select_kernel",
@@ -113,6 +115,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
         lib = ctypes.CDLL(p)
         lib.mfa_fwd.argtypes = [ctypes.POINTER(MfaFwdParams), ctypes.c_void_p]
         lib.mfa_fwd.restype = ctypes.c_int
+        lib.mfa_fwd_noalloc.argtypes = [ctypes.POINTER(MfaFwdParams), ctypes.c_void_p]
+        lib.mfa_fwd_noalloc.restype = ctypes.c_int
         lib.mfa_fwd_workspace_size.argtypes = [ctypes.POINTER(MfaFwdParams)]
         lib.mfa_fwd_workspace_size.restype = ctypes.c_size_t
         lib.mfa_fwd_num_splits.argtypes = [ctypes.POINTER(MfaFwdParams)]
@@ -146,6 +150,10 @@ def status_string(status: int) -> str:
 
 def fwd(params: MfaFwdParams, stream: int) -> int:
     return load().mfa_fwd(ctypes.byref(params), ctypes.c_void_p(stream))
+
+
+def fwd_noalloc(params: MfaFwdParams, stream: int) -> int:
+    return load().mfa_fwd_noalloc(ctypes.byref(params), ctypes.c_void_p(stream))
 
 
 def workspace_size(params: MfaFwdParams) -> int:

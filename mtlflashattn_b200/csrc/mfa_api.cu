@@ -350,6 +350,30 @@ int run_simt(const mfa_fwd_params* p, FwdArgs a, cudaStream_t st) {
 #undef MFA_SIMT
 }
 
+// ------------------------------------------------------------------ no-allocation variant
+// Scratch for mfa_fwd_noalloc: the split-KV partials live in this fixed device array instead of
+// a caller-provided workspace. Every GPU that loads the library holds it until the process
+// exits. Host code must not pass the symbol itself to a kernel (on the host it only names a
+// shadow variable); noalloc_scratch() resolves its device address for the current device.
+constexpr size_t kNoAllocScratchBytes = 16u << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on `dev` (the current device), looked up once per device.
+int noalloc_scratch(int dev, void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  if (dev < 0 || dev >= 64) return MFA_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lk(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
+      return MFA_ERR_CUDA;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return MFA_OK;
+}
+
 }  // namespace
 }  // namespace mfa
 
@@ -366,6 +390,8 @@ const char* mfa_status_string(int s) {
     case MFA_ERR_TIMEOUT: return "in-kernel wait timed out";
     case MFA_ERR_NO_DEVICE: return "no usable CUDA device";
     case MFA_ERR_FAULT_INJECTED: return "fault injected (MFA_FAULT)";
+    case MFA_ERR_SCRATCH_TOO_SMALL:
+      return "problem needs more split-KV scratch than mfa_fwd_noalloc's fixed 16 MiB buffer";
     default: return "unknown status";
   }
 }
@@ -418,6 +444,26 @@ int mfa_fwd(const mfa_fwd_params* p, void* stream) {
                                   : mfa::run_simt(p, a, st);
   if (rc != MFA_OK) return rc;
   return cudaGetLastError() == cudaSuccess ? MFA_OK : MFA_ERR_CUDA;
+}
+
+int mfa_fwd_noalloc(const mfa_fwd_params* p, void* stream) {
+  if (p == nullptr) return MFA_ERR_INVALID;
+  int rc = mfa::validate(p);
+  if (rc != MFA_OK) return rc;
+  mfa_fwd_params q = *p;  // same call, with the library's own scratch as the workspace
+  q.workspace = nullptr;
+  q.workspace_bytes = 0;
+  const size_t need = mfa_fwd_workspace_size(&q);
+  if (need > 0) {
+    if (need > mfa::kNoAllocScratchBytes) return MFA_ERR_SCRATCH_TOO_SMALL;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return MFA_ERR_NO_DEVICE;
+    void* scratch = nullptr;
+    if ((rc = mfa::noalloc_scratch(dev, &scratch)) != MFA_OK) return rc;
+    q.workspace = scratch;
+    q.workspace_bytes = mfa::kNoAllocScratchBytes;
+  }
+  return mfa_fwd(&q, stream);
 }
 
 int mfa_lse_combine(const float* const* o_part, const float* const* lse_part, int32_t n,

@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol():
 def test_abi_version_and_status_strings():
     lib = _lib.load()
     assert lib.mfa_abi_version() == _lib.MFA_ABI_VERSION
-    for s in range(7):
+    for s in range(8):
         assert _lib.status_string(s)
     assert _lib.status_string(0) == "ok"
 
