@@ -136,6 +136,13 @@ int mfa_lse_combine(const float* const* o_part, const float* const* lse_part, in
                     int32_t rows, int32_t H, int32_t D, void* o, int32_t o_dtype,
                     float* lse, void* cuda_stream);
 
+/* Failure-detection self-test (no counterpart in the reference): launches one thread that waits
+ * on an mbarrier nothing arrives on, with the same bounded wait the attention kernels use but a
+ * limit of timeout_us microseconds, and stores MFA_ERR_TIMEOUT (or 0) in the device int *err.
+ * Shows that a stalled wait ends with a status the host can read and leaves the context usable;
+ * it faults, traps or hangs nothing. */
+int mfa_selftest_wait_timeout(int32_t* err, uint32_t timeout_us, void* cuda_stream);
+
 const char* mfa_status_string(int status);
 int mfa_abi_version(void);
 

@@ -40,6 +40,7 @@ EXPORTED_SYMBOLS = (
     "mfa_fwd_num_splits",
     "mfa_select_kernel",
     "mfa_lse_combine",
+    "mfa_selftest_wait_timeout",
     "mfa_status_string",
     "mfa_abi_version",
 )
@@ -129,6 +130,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
             ctypes.c_void_p, ctypes.c_void_p,
         ]
         lib.mfa_lse_combine.restype = ctypes.c_int
+        lib.mfa_selftest_wait_timeout.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]
+        lib.mfa_selftest_wait_timeout.restype = ctypes.c_int
         lib.mfa_status_string.argtypes = [ctypes.c_int]
         lib.mfa_status_string.restype = ctypes.c_char_p
         lib.mfa_abi_version.argtypes = []

@@ -8,6 +8,7 @@
 // tier (metal_flash_attn/_kernel.py:1165-1208) and of its scalar v0 kernel (_kernel.py:32-87).
 #pragma once
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace mfa {
 namespace simt {
@@ -231,6 +232,20 @@ __global__ void split_combine_kernel(const FwdArgs a, const float* __restrict__ 
     }
   }
   if (lane == 0 && lse_out != nullptr) lse_out[(int64_t)b * a.lse_sb + (int64_t)h * a.lse_sh + row] = lse;
+}
+
+// Self-test of the bounded wait every pipelined kernel uses: one thread waits on an mbarrier
+// that nothing ever arrives on, gives up after `timeout_ns` of device time and reports
+// MFA_ERR_TIMEOUT (4) in *err, exactly as a stalled attention CTA does. No fault, trap or hang.
+__global__ void wait_timeout_selftest(int* err, uint64_t timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x != 0) return;
+  abort_flag = 0;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  const bool ok = mbar_wait(&bar, 0, &abort_flag, timeout_ns);
+  *err = ok ? 0 : 4;
 }
 
 }  // namespace mfa

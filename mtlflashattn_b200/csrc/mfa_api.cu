@@ -466,6 +466,14 @@ int mfa_fwd_noalloc(const mfa_fwd_params* p, void* stream) {
   return mfa_fwd(&q, stream);
 }
 
+int mfa_selftest_wait_timeout(int32_t* err, uint32_t timeout_us, void* stream) {
+  if (err == nullptr || timeout_us == 0 || timeout_us > 10000000u) return MFA_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  (void)cudaGetLastError();
+  mfa::wait_timeout_selftest<<<1, 32, 0, st>>>(err, (uint64_t)timeout_us * 1000ull);
+  return cudaGetLastError() == cudaSuccess ? MFA_OK : MFA_ERR_CUDA;
+}
+
 int mfa_lse_combine(const float* const* o_part, const float* const* lse_part, int32_t n,
                     int32_t rows, int32_t H, int32_t D, void* o, int32_t o_dtype, float* lse,
                     void* stream) {
