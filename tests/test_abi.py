@@ -82,3 +82,9 @@ def test_fault_injection_fires_before_launch(monkeypatch):
 def test_combine_argument_checks():
     assert _lib.lse_combine([0] * 65, [0] * 65, 1, 1, 1, 0, 0, 0, 0) == _lib.ERR_INVALID
     assert _lib.lse_combine([0], [0], 0, 1, 1, 0, 0, 0, 0) == _lib.OK
+
+
+def test_wait_selftest_argument_checks():
+    lib = _lib.load()
+    assert lib.mfa_selftest_wait_timeout(None, 1000, None) == _lib.ERR_INVALID
+    assert lib.mfa_selftest_wait_timeout(None, 0, None) == _lib.ERR_INVALID
