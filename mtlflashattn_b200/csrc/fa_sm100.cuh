@@ -21,7 +21,9 @@
 // The MMA warp issues, per key block j:  PV0_j, S0_{j+1}, PV1_j, S1_{j+1}.  tcgen05 MMAs of
 // one thread execute in issue order, so S_t(j+1) never overwrites P_t(j) before PV_t(j) read it,
 // and the commit that publishes S_t(j+1) also covers PV_t(j); that is what lets the softmax
-// warps rescale O_t in place right after they see S_t(j+1). (A variant that released S_t to the
+// warps rescale O_t in place right after they see S_t(j+1). With CG = 1 the softmax publishes P_t in
+// two key halves on separate mbarriers and the MMA warp issues the first four P.V MMAs while
+// the second half is still being computed (measured +5% on the plain path; quarters: +1-3%). (A variant that released S_t to the
 // MMA as soon as it was in registers, with P in separate TMEM columns or shared memory and an
 // event-driven issuer, measured 5-20% slower on every BASELINE configuration.)
 //
@@ -107,6 +109,9 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 #ifndef MFA_CG_PLAIN
 #define MFA_CG_PLAIN 1
 #endif
+#ifndef MFA_PPARTS
+#define MFA_PPARTS 2
+#endif
 template <bool kGeneral>
 struct DefaultCG {
   static constexpr int value = kGeneral ? 2 : MFA_CG_PLAIN;
@@ -125,6 +130,9 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
   constexpr int kSoftmaxRegs = R::kSoftmaxRegs;
   constexpr int kOtherRegs = R::kOtherRegs;
   constexpr int NC = R::NC;
+  // P_t is published to the MMA in this many key parts (one part with CG = 2, where both
+  // column groups' halves are needed before the P.V MMAs of a part could start anyway).
+  constexpr int kPParts = CG == 1 ? MFA_PPARTS : 1;
   const FwdArgs& a = args.a;
 
   extern __shared__ uint8_t smem_raw[];
@@ -137,8 +145,8 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
   uint64_t* kv_full = bars + 2;            // [NSLOT]
   uint64_t* kv_empty = kv_full + C::NSLOT; // [NSLOT]
   uint64_t* s_full = kv_empty + C::NSLOT;  // [2]
-  uint64_t* p_full = s_full + 2;           // [2]
-  uint64_t* o_full = p_full + 2;           // [2]
+  uint64_t* p_full = s_full + 2;           // [2][kPParts]: tile, key part
+  uint64_t* o_full = p_full + 2 * kPParts; // [2]
   uint64_t* s_free = o_full + 2;           // [2] decoupled only
   uint64_t* pv_done = s_free + 2;          // [2] decoupled only
   uint64_t* mma_done = pv_done + 2;        // [1]
@@ -182,7 +190,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 4 * CG);
+      for (int q = 0; q < kPParts; ++q) mbar_init(&p_full[kPParts * t + q], 4 * CG);
       mbar_init(&o_full[t], 1);
       mbar_init(&s_free[t], 4 * CG);
       mbar_init(&pv_done[t], 1);
@@ -260,13 +268,21 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
           mma_ss(d, a0 + koff, b0 + koff, kIdQK, k > 0);
         }
       };
-      auto pv = [&](int t, int it, bool acc) {  // O_t (+)= P_t V, V in ring item `it`
+      // O_t (+)= P_t V, V in ring item `it`. P_t arrives in kPParts key parts; the MMAs of a
+      // part run while the softmax is still producing the next one.
+      auto pv = [&](int t, int it, bool acc, int j) {
         const uint64_t b0 = dV + (((it % C::NSLOT) * C::TILE) >> 4);
         const uint32_t d = tmem + 256u + DP * t;
         const uint32_t pa = tmem + (C::DECOUPLED ? C::TMEM_P + 64u * t : 128u * t);
 #pragma unroll
-        for (int k = 0; k < BN / 16; ++k)
-          mma_ts(d, pa + k * 8, b0 + ((k * 2048) >> 4), kIdPV, (acc || k > 0) ? 1u : 0u);
+        for (int q = 0; q < kPParts; ++q) {
+          if (!mbar_wait(&p_full[kPParts * t + q], (uint32_t)j & 1u, abort_flag)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int k = q * (8 / kPParts); k < (q + 1) * (8 / kPParts); ++k)
+            mma_ts(d, pa + k * 8, b0 + ((k * 2048) >> 4), kIdPV, (acc || k > 0) ? 1u : 0u);
+        }
+        return true;
       };
       auto ring_wait = [&](int it) {
         return mbar_wait(&kv_full[it % C::NSLOT], (uint32_t)(it / C::NSLOT) & 1u, abort_flag);
@@ -299,14 +315,10 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
             tc_commit(&s_full[1]);
             tc_commit(&kv_empty[itK % C::NSLOT]);
           }
-          ok = ring_wait(itV) && mbar_wait(&p_full[0], (uint32_t)j & 1u, abort_flag);
+          ok = ring_wait(itV) && pv(0, itV, j > 0, j);
           if (!ok) break;
-          tc_fence_after();
-          pv(0, itV, j > 0);
           tc_commit(&pv_done[0]);
-          if (!(ok = mbar_wait(&p_full[1], (uint32_t)j & 1u, abort_flag))) break;
-          tc_fence_after();
-          pv(1, itV, j > 0);
+          if (!(ok = pv(1, itV, j > 0, j))) break;
           tc_commit(&pv_done[1]);
           tc_commit(&kv_empty[itV % C::NSLOT]);
         }
@@ -314,10 +326,8 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
       for (int j = 0; j < n && ok; ++j) {
         const int itV = 2 * j + 1, itK = 2 * j + 2;
         const bool more = j + 1 < n;
-        ok = ring_wait(itV) && mbar_wait(&p_full[0], (uint32_t)j & 1u, abort_flag);
+        ok = ring_wait(itV) && pv(0, itV, j > 0, j);
         if (!ok) break;
-        tc_fence_after();
-        pv(0, itV, j > 0);
         if (!more) tc_commit(&o_full[0]);
         if (more) {
           if (!(ok = ring_wait(itK))) break;
@@ -325,9 +335,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
           qk(0, itK);
           tc_commit(&s_full[0]);
         }
-        if (!(ok = mbar_wait(&p_full[1], (uint32_t)j & 1u, abort_flag))) break;
-        tc_fence_after();
-        pv(1, itV, j > 0);
+        if (!(ok = pv(1, itV, j > 0, j))) break;
         tc_commit(&kv_empty[itV % C::NSLOT]);
         if (!more) tc_commit(&o_full[1]);
         if (more) {
@@ -512,6 +520,14 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
         }
         // P_t: its own columns (decoupled) or over the first 64 columns of S_t
         tmem_st16((C::DECOUPLED ? tmem + lane_base + C::TMEM_P + t * 64 : tS) + col0 / 2 + 16 * cc, pk);
+        if constexpr (kPParts > 1) {
+          if ((cc + 1) % (NC / 32 / kPParts) == 0 && cc + 1 < NC / 32) {  // an early part
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[kPParts * t + (cc + 1) / (NC / 32 / kPParts) - 1]);
+          }
+        }
       }
       float la, lb;
       f2unpack(fadd2(acc0, acc1), la, lb);
@@ -519,7 +535,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
+      if (lane == 0) mbar_arrive(&p_full[kPParts * t + kPParts - 1]);
     }
     if (ok && n > 0) {
       ok = __all_sync(kFull, C::DECOUPLED
