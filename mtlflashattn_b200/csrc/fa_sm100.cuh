@@ -412,8 +412,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
           if (cap > 0.f) {
             float ya, yb;
             f2unpack(fmul2(s2, f2pack(sc_in, sc_in)), ya, yb);
-            ya = fminf(fmaxf(ya, -43.f), 43.f);  // |tanh| = 1 in fp32 beyond 2*log2e*15
-            yb = fminf(fmaxf(yb, -43.f), 43.f);
+            // no clamp needed: 2^y overflows to +inf -> rcp = 0 -> tanh = 1; 2^y -> 0 -> tanh = -1
             const uint64_t e2 = fadd2(f2pack(ex2(ya), ex2(yb)), f2pack(1.f, 1.f));
             float ea, eb;
             f2unpack(e2, ea, eb);
