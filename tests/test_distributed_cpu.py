@@ -93,15 +93,18 @@ def _dead_rank_worker(rank, world, port, result_q):
     """Rank 1 leaves before the merge; rank 0's collective must end with an error, not hang."""
     import datetime
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=5))
-    if rank == 1:
-        os._exit(0)
     try:
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=5))
+        if rank == 1:
+            os._exit(0)
         mfd.merge_partials(torch.zeros(1, 4, 2, 8), torch.zeros(1, 2, 4))
         result_q.put("no-error")
-    except Exception as e:  # noqa: BLE001
-        result_q.put(type(e).__name__)
+    except Exception as e:  # noqa: BLE001 - init or the collective saw the missing rank
+        if rank == 0:
+            result_q.put(type(e).__name__)
+    result_q.close()
+    result_q.join_thread()  # flush the queue's feeder thread before the hard exit
     os._exit(0)
 
 
