@@ -104,23 +104,32 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 #ifndef MFA_EMU128
 #define MFA_EMU128 0
 #endif
-// Column groups per tile; see the role table above. Measured on B200: the softcap / ALiBi path
-// (more work per score) gains 17-29% from CG = 2, the plain path loses 9-17%.
+// Score transform, a template parameter of the kernel:
+//   kBias = 0  x = s                        (c = scale*log2e folded into the exponent)
+//   kBias = 1  x = log2e*(s*scale - slope*|centre - key|)   (any scale, ALiBi optional)
+//   kBias = 2  x = log2e*(softcap(s*scale) - slope*|centre - key|)
+// Column groups per tile; see the role table above. Measured on B200: the softcap and ALiBi
+// paths gain from CG = 2 (ALiBi-only: +17% over CG = 1), the plain path loses 9-17%. Separate
+// kBias = 1 / 2 kernels (rather than one kernel testing softcap at run time) cut the CG = 2
+// register spills and gained 11-13% on the softcap and ALiBi configurations.
 #ifndef MFA_CG_PLAIN
 #define MFA_CG_PLAIN 1
+#endif
+#ifndef MFA_CG_LINEAR
+#define MFA_CG_LINEAR 2
 #endif
 #ifndef MFA_PPARTS
 #define MFA_PPARTS 2
 #endif
-template <bool kGeneral>
+template <int kBias>
 struct DefaultCG {
-  static constexpr int value = kGeneral ? 2 : MFA_CG_PLAIN;
+  static constexpr int value = kBias == 2 ? 2 : kBias == 1 ? MFA_CG_LINEAR : MFA_CG_PLAIN;
 };
 __device__ __forceinline__ void named_barrier(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-template <int DP, bool kBF16, bool kGeneral, int CG = DefaultCG<kGeneral>::value,
+template <int DP, bool kBF16, int kBias, int CG = DefaultCG<kBias>::value,
           int kEmu = (DP == 64 ? MFA_EMU64 : MFA_EMU128)>
 __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
     fa_fwd_sm100(const __grid_constant__ Sm100Args args) {
@@ -134,6 +143,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
   // column groups' halves are needed before the P.V MMAs of a part could start anyway).
   constexpr int kPParts = CG == 1 ? MFA_PPARTS : 1;
   const FwdArgs& a = args.a;
+  constexpr bool kGeneral = kBias != 0;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -409,7 +419,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
         for (int i = 0; i < NC; i += 2) {
           uint64_t s2 = f2pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
           uint64_t x2;
-          if (cap > 0.f) {
+          if constexpr (kBias == 2) {
             float ya, yb;
             f2unpack(fmul2(s2, f2pack(sc_in, sc_in)), ya, yb);
             // no clamp needed: 2^y overflows to +inf -> rcp = 0 -> tanh = 1; 2^y -> 0 -> tanh = -1

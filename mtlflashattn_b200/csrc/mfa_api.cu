@@ -233,7 +233,7 @@ int make_map(CUtensorMap* m, const void* base, int dtype, int D, int H, int64_t 
   return r == CUDA_SUCCESS ? MFA_OK : MFA_ERR_CUDA;
 }
 
-template <int DP, bool BF16, bool GEN>
+template <int DP, bool BF16, int GEN>
 int launch_sm100(const Sm100Args& args, int dev, int64_t grid, cudaStream_t st) {
   auto k = fa_fwd_sm100<DP, BF16, GEN>;
   const int smem = (int)sm100::Cfg<DP>::SMEM;
@@ -306,7 +306,7 @@ int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
   const int64_t grid = (int64_t)a.num_row_blocks * a.Hq * a.B * a.num_splits;
   if (grid == 0) return MFA_OK;
   if (grid >= (1ll << 31)) return MFA_ERR_UNSUPPORTED;
-  const bool gen = !(a.scale > 0.f) || a.softcap > 0.f || a.alibi != nullptr;
+  const int gen = a.softcap > 0.f ? 2 : (!(a.scale > 0.f) || a.alibi != nullptr) ? 1 : 0;
   const bool bf = p->dtype == MFA_BF16;
   const bool wide = p->D > 64;
 #define MFA_SM100(DP, BF, G)                                                     \
@@ -316,13 +316,23 @@ int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
     return launch_combine(fin, ws_o, ws_lse, p->o, p->lse, st);                  \
   } while (0)
   if (wide) {
-    if (bf) { if (gen) MFA_SM100(128, true, true); MFA_SM100(128, true, false); }
-    if (gen) MFA_SM100(128, false, true);
-    MFA_SM100(128, false, false);
+    if (bf) {
+      if (gen == 2) MFA_SM100(128, true, 2);
+      if (gen == 1) MFA_SM100(128, true, 1);
+      MFA_SM100(128, true, 0);
+    }
+    if (gen == 2) MFA_SM100(128, false, 2);
+    if (gen == 1) MFA_SM100(128, false, 1);
+    MFA_SM100(128, false, 0);
   }
-  if (bf) { if (gen) MFA_SM100(64, true, true); MFA_SM100(64, true, false); }
-  if (gen) MFA_SM100(64, false, true);
-  MFA_SM100(64, false, false);
+  if (bf) {
+    if (gen == 2) MFA_SM100(64, true, 2);
+    if (gen == 1) MFA_SM100(64, true, 1);
+    MFA_SM100(64, true, 0);
+  }
+  if (gen == 2) MFA_SM100(64, false, 2);
+  if (gen == 1) MFA_SM100(64, false, 1);
+  MFA_SM100(64, false, 0);
 #undef MFA_SM100
 }
 
