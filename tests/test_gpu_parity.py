@@ -170,6 +170,29 @@ def test_kernels_agree_random_shapes(shape, dtype, causal):
         check_close(out, want, dtype, f"{shape} {kern}")
 
 
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("causal", [False, True])
+def test_row_max_jumps_in_later_key_blocks(D, dtype, causal):
+    """Keys far later in the sequence whose logits jump by 6-35 (natural units) over everything
+    before them, placed in both key halves of their 128-key blocks: the kernel's running row
+    maximum must grow mid-sequence (rescaling O and the row sum), including after the first
+    half of a block has already been handed to the P.V MMAs."""
+    B, L, H = 1, 1024, 2
+    q, k, v = ref.make_qkv(B, L, L, H, H, D, torch.float32, seed=D + causal)
+    u = torch.nn.functional.normalize(torch.randn(D, generator=torch.Generator().manual_seed(1)),
+                                      dim=0)
+    q = q + 2.0 * u  # every query row leans along u
+    for key, jump in ((200, 6.0), (500, 12.0), (700, 20.0), (900, 35.0), (1000, 45.0)):
+        k[:, key] = u * (jump * math.sqrt(D) / 2.0)  # logit ~ jump over the rest
+    q, k, v = q.to(dtype), k.to(dtype), v.to(dtype)
+    want = ref.flash_attn_func(q, k, v, causal=causal)
+    with pytest.MonkeyPatch.context() as mp:
+        mp.setenv("MTLFLASHATTN_KERNEL", "tcgen05")
+        out = mfa.flash_attn_func(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+    check_close(out, want, dtype, f"jumps D={D} {dtype} causal={causal}")
+
+
 def test_empty_and_degenerate_shapes():
     for (B, Lq, Lk) in ((0, 16, 16), (1, 0, 16), (1, 16, 0)):
         q, k, v = ref.make_qkv(max(B, 1), Lq, Lk, 2, 2, 64, torch.bfloat16)
