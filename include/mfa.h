@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define MFA_ABI_VERSION 2
+#define MFA_ABI_VERSION 3
 
 /* Status codes. The Python layer maps them to the reference's exception types. */
 enum mfa_status {
@@ -135,6 +135,28 @@ int mfa_select_kernel(const mfa_fwd_params* p);
 int mfa_lse_combine(const float* const* o_part, const float* const* lse_part, int32_t n,
                     int32_t rows, int32_t H, int32_t D, void* o, int32_t o_dtype,
                     float* lse, void* cuda_stream);
+
+/* Host buffers of mfa_fwd_staged. */
+typedef struct {
+  const void *q, *k, *v; /* inputs in host memory (pinned for overlap), laid out with the same
+                            strides as the device buffers p->q, p->k, p->v */
+  void* o;               /* output in host memory, same strides as p->o */
+  const int32_t* cu_q;   /* varlen only: host copies of p->cu_q / p->cu_k ([B + 1]) */
+  const int32_t* cu_k;
+  int32_t chunks;        /* pipeline pieces: 0 = automatic (each piece at least one wave of
+                            256-row CTAs, at most 16), 1 = copy, compute, copy back */
+} mfa_host_io;
+
+/* Forward of host-resident inputs into a host-resident output (no counterpart in the
+ * reference, whose tensors live on the device already). p describes the problem and names
+ * device buffers of the same layout that serve as staging areas (p->lse, if set, stays on the
+ * device). The problem is cut into pieces: runs of query rows of each batch (each needing only
+ * the key prefix its last row can attend: causal and right-windowed inputs start computing
+ * before all keys have arrived) or runs of whole varlen sequences. The host-to-device copy of
+ * piece c+1, the forward of piece c and the device-to-host copy of piece c-1 overlap, on two
+ * internal streams joined to cuda_stream by events: when the call's work on cuda_stream is
+ * complete, io->o holds the result. Results equal one mfa_fwd call on the whole problem. */
+int mfa_fwd_staged(const mfa_fwd_params* p, const mfa_host_io* io, void* cuda_stream);
 
 /* Failure-detection self-test (no counterpart in the reference): launches one thread that waits
  * on an mbarrier nothing arrives on, with the same bounded wait the attention kernels use but a

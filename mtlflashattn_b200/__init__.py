@@ -15,6 +15,7 @@ import torch
 from ._kernel import MAX_HEAD_DIM, _BiasParams, _broadcast_alibi_slopes, flash_attn_forward
 from . import _kernel
 from ._version import __version__
+from .host import flash_attn_host, flash_attn_varlen_host
 
 __all__ = [
     "flash_attn_func",
@@ -24,6 +25,8 @@ __all__ = [
     "flash_attn_varlen_qkvpacked_func",
     "flash_attn_varlen_kvpacked_func",
     "flash_attn_forward",
+    "flash_attn_host",
+    "flash_attn_varlen_host",
     "__version__",
 ]
 

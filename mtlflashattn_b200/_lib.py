@@ -13,7 +13,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmfa.so")
 
-MFA_ABI_VERSION = 2
+MFA_ABI_VERSION = 3
 
 # mfa_status
 OK = 0
@@ -36,6 +36,7 @@ KERNEL_NAMES = {KERNEL_TCGEN05: "tcgen05", KERNEL_SIMT: "simt"}
 EXPORTED_SYMBOLS = (
     "mfa_fwd",
     "mfa_fwd_noalloc",
+    "mfa_fwd_staged",
     "mfa_fwd_workspace_size",
     "mfa_fwd_num_splits",
     "mfa_select_kernel",
@@ -87,6 +88,20 @@ class MfaFwdParams(ctypes.Structure):
     ]
 
 
+class MfaHostIo(ctypes.Structure):
+    """Mirror of ``struct mfa_host_io`` (include/mfa.h)."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("o", ctypes.c_void_p),
+        ("cu_q", ctypes.c_void_p),
+        ("cu_k", ctypes.c_void_p),
+        ("chunks", ctypes.c_int32),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -118,6 +133,9 @@ def load(path: str | None = None) -> ctypes.CDLL:
         lib.mfa_fwd.restype = ctypes.c_int
         lib.mfa_fwd_noalloc.argtypes = [ctypes.POINTER(MfaFwdParams), ctypes.c_void_p]
         lib.mfa_fwd_noalloc.restype = ctypes.c_int
+        lib.mfa_fwd_staged.argtypes = [ctypes.POINTER(MfaFwdParams), ctypes.POINTER(MfaHostIo),
+                                        ctypes.c_void_p]
+        lib.mfa_fwd_staged.restype = ctypes.c_int
         lib.mfa_fwd_workspace_size.argtypes = [ctypes.POINTER(MfaFwdParams)]
         lib.mfa_fwd_workspace_size.restype = ctypes.c_size_t
         lib.mfa_fwd_num_splits.argtypes = [ctypes.POINTER(MfaFwdParams)]
@@ -157,6 +175,10 @@ def fwd(params: MfaFwdParams, stream: int) -> int:
 
 def fwd_noalloc(params: MfaFwdParams, stream: int) -> int:
     return load().mfa_fwd_noalloc(ctypes.byref(params), ctypes.c_void_p(stream))
+
+
+def fwd_staged(params: MfaFwdParams, io: MfaHostIo, stream: int) -> int:
+    return load().mfa_fwd_staged(ctypes.byref(params), ctypes.byref(io), ctypes.c_void_p(stream))
 
 
 def workspace_size(params: MfaFwdParams) -> int:

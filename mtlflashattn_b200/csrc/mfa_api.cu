@@ -10,6 +10,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "../../include/mfa.h"
 #include "fa_simt.cuh"
@@ -384,6 +385,8 @@ int noalloc_scratch(int dev, void** out) {
   return MFA_OK;
 }
 
+#include "staged.inc"
+
 }  // namespace
 }  // namespace mfa
 
@@ -474,6 +477,14 @@ int mfa_fwd_noalloc(const mfa_fwd_params* p, void* stream) {
     q.workspace_bytes = mfa::kNoAllocScratchBytes;
   }
   return mfa_fwd(&q, stream);
+}
+
+int mfa_fwd_staged(const mfa_fwd_params* p, const mfa_host_io* io, void* stream) {
+  if (mfa::fault_injected("fwd")) return MFA_ERR_FAULT_INJECTED;
+  if (io == nullptr) return MFA_ERR_INVALID;
+  int rc = mfa::validate(p);
+  if (rc != MFA_OK) return rc;
+  return mfa::run_staged(p, io, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int mfa_selftest_wait_timeout(int32_t* err, uint32_t timeout_us, void* stream) {

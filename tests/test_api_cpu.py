@@ -175,3 +175,16 @@ def test_shim_finder_gated_on_cuda():
     spec = _finder._MtlFlashAttnB200Finder().find_spec("flash_attn")
     assert (spec is not None) == torch.cuda.is_available()
     assert _finder._MtlFlashAttnB200Finder().find_spec("numpy") is None
+
+
+def test_host_api_argument_errors():
+    q = torch.zeros(1, 8, 2, 64, dtype=torch.int32)
+    with pytest.raises(NotImplementedError):
+        mfa.flash_attn_host(q, q, q)
+    q = torch.zeros(1, 8, 2, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        mfa.flash_attn_host(q, q, q, window_size=(-2, 0))
+    with pytest.raises(ValueError):
+        mfa.flash_attn_host(q, q, q, softcap=-1.0)
+    with pytest.raises(NotImplementedError):
+        mfa.flash_attn_host(torch.zeros(1, 8, 2, 160, dtype=torch.bfloat16), q, q)
