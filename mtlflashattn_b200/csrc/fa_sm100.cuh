@@ -118,6 +118,11 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 #ifndef MFA_CG_LINEAR
 #define MFA_CG_LINEAR 2
 #endif
+// Softcap: of every 8 pairs of scores, how many take the reciprocal on the FMA pipe (Newton)
+// instead of MUFU.RCP; 2 balances the pipes best on B200 (+1.5% on config 3, 8: -5%).
+#ifndef MFA_RCP_EMU
+#define MFA_RCP_EMU 2
+#endif
 #ifndef MFA_PPARTS
 #define MFA_PPARTS 2
 #endif
@@ -426,7 +431,22 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
             const uint64_t e2 = fadd2(f2pack(ex2(ya), ex2(yb)), f2pack(1.f, 1.f));
             float ea, eb;
             f2unpack(e2, ea, eb);
-            x2 = ffma2(f2pack(rcp(ea), rcp(eb)), f2pack(sc_b, sc_b), f2pack(sc_a, sc_a));
+            uint64_t r2;
+            if (((i >> 1) & 7) < MFA_RCP_EMU) {
+              // reciprocal on the FMA pipe: bit-trick guess (relative error < 1/8) and three
+              // Newton steps r += r(1 - d r) (error < 1e-7); d >= 1 is clamped below 2^126 so the
+              // guess stays a normal number (1/d < 1.2e-38 is 0 for the logit anyway)
+              ea = fminf(ea, 8.5e37f);
+              eb = fminf(eb, 8.5e37f);
+              const uint64_t nd = f2pack(-ea, -eb), one = f2pack(1.f, 1.f);
+              r2 = f2pack(__int_as_float(0x7EF311C3 - __float_as_int(ea)),
+                          __int_as_float(0x7EF311C3 - __float_as_int(eb)));
+#pragma unroll
+              for (int it = 0; it < 3; ++it) r2 = ffma2(r2, ffma2(nd, r2, one), r2);
+            } else {
+              r2 = f2pack(rcp(ea), rcp(eb));
+            }
+            x2 = ffma2(r2, f2pack(sc_b, sc_b), f2pack(sc_a, sc_a));
           } else {
             x2 = fmul2(s2, f2pack(pl_scale, pl_scale));
           }
