@@ -2,7 +2,10 @@
 // accumulators -> fp32 online softmax in registers -> P -> P.V on tcgen05.
 //
 // One CTA owns 256 query rows of one (batch, head) as two 128-row tiles (t = 0, 1) and streams
-// the key/value blocks (128 keys each) that any of those rows may attend.
+// the key/value blocks (128 keys each) that any of those rows may attend. For D = 64 without
+// softcap / ALiBi a CTA owns one 128-row tile (TILES = 1) and two CTAs share each SM: their
+// MMA warps issue independently, so the two tiles' softmax phases do not run in lock-step
+// (+1.4% on B=1 H=16 L=8192 causal, +2.7% with 1 of 8 exponential pairs on the FMA pipe).
 //
 //   warpgroups 0 .. 2*CG-1   softmax: tile t = wg / CG, key columns [cg*128/CG, (cg+1)*128/CG)
 //                            with cg = wg % CG (TMEM lanes 0-127, one query row per thread)
@@ -47,35 +50,43 @@ namespace sm100 {
 constexpr int BM = 128;  // query rows per tile (TMEM lanes)
 constexpr int BN = 128;  // keys per block
 
-// Thread roles and register budget for CG column groups per tile.
-template <int CG>
+// Thread roles and register budget for CG column groups per tile and TILES 128-row tiles per
+// CTA. TILES = 1 CTAs are sized so that two of them share an SM (half the TMEM columns, half
+// the registers, under half the shared memory).
+template <int CG, int TILES = 2>
 struct Roles {
-  static constexpr int kSoftWarps = 8 * CG;
+  static_assert(TILES == 2 || CG == 1, "one-tile CTAs use one column group");
+  static constexpr int kSoftWarps = 4 * CG * TILES;
   static constexpr int kProducer = kSoftWarps;
   static constexpr int kMma = kSoftWarps + 1;
-  static constexpr int kThreads = 128 * (2 * CG + 1);
-  // registers per thread at launch: the register file of one SM sub-partition (16384) over the
-  // warps it holds, rounded down to a multiple of 8
-  static constexpr int kLaunchRegs = CG == 1 ? 168 : 96;
-  static constexpr int kSoftmaxRegs = CG == 1 ? 208 : 104;
-  static constexpr int kOtherRegs = CG == 1 ? 88 : 64;
+  static constexpr int kThreads = 128 * (TILES * CG + 1);
+  static constexpr int kCtasPerSm = TILES == 1 ? 2 : 1;
+  // registers per thread at launch: the register file (65536) over the threads of the CTAs
+  // that share an SM, rounded down to a multiple of 8
+  static constexpr int kLaunchRegs = (65536 / (kThreads * kCtasPerSm)) / 8 * 8;
+  static constexpr int kSoftmaxRegs = TILES == 1 ? 184 : CG == 1 ? 208 : 104;
+  static constexpr int kOtherRegs = TILES == 1 ? 72 : CG == 1 ? 88 : 64;
   static constexpr int NC = 128 / CG;  // score columns per softmax thread
-  static_assert(2 * CG * 128 * kSoftmaxRegs + 128 * kOtherRegs <= kThreads * kLaunchRegs,
+  static_assert(TILES * CG * 128 * kSoftmaxRegs + 128 * kOtherRegs <= kThreads * kLaunchRegs,
                 "setmaxnreg split exceeds the launch register budget");
 };
 
-template <int DP>
+template <int DP, int TILES = 2>
 struct Cfg {
   static constexpr int NCH = DP / 64;                    // 128-byte column chunks per row
   static constexpr uint32_t CHUNK = 128u * 128u;         // one chunk of 128 rows: 16 KB
   static constexpr uint32_t TILE = NCH * CHUNK;          // Q tile or K / V block
-  static constexpr int NSLOT = DP == 128 ? 3 : 6;        // K/V ring depth
-  static constexpr uint32_t BAR_OFF = 2 * TILE + NSLOT * TILE;
-  static constexpr uint32_t XCH_OFF = BAR_OFF + 256;
-  // D = 64 leaves TMEM columns [384, 512) free: P gets its own columns and S is released to the
-  // MMA as soon as it is in registers (see "decoupled" below). D = 128 aliases P over S.
+  static constexpr int NSLOT = DP == 128 ? 3 : TILES == 1 ? 5 : 6;  // K/V ring depth
+  static constexpr uint32_t BAR_OFF = TILES * TILE + NSLOT * TILE;
+  static constexpr uint32_t XCH_OFF = BAR_OFF + 256;     // [parity][tile][cg][row] fp32 (CG = 2)
+  // TMEM columns: S_t at 128 t, O_t at TMEM_O + DP t, and (decoupled) P_t at TMEM_P + 64 t.
+  // D = 64 leaves room for P in its own columns and S is released to the MMA as soon as it is
+  // in registers (see "decoupled" below). D = 128 aliases P over S.
   static constexpr bool DECOUPLED = DP == 64;
-  static constexpr uint32_t TMEM_P = 384;  // [parity][tile][cg][row] fp32 exchange
+  static_assert(TILES == 2 || DECOUPLED, "one-tile CTAs use the decoupled protocol");
+  static constexpr uint32_t TMEM_O = 128u * TILES;
+  static constexpr uint32_t TMEM_P = 128u * TILES + (uint32_t)DP * TILES;
+  static constexpr uint32_t TMEM_COLS = TILES == 1 ? 256 : 512;
   static constexpr uint32_t SMEM = XCH_OFF + 4096 + 1024;  // + alignment slack
 };
 
@@ -99,7 +110,7 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 // kEmu: of every 8 pairs of probabilities, how many are computed with exp2_poly2 on the FMA
 // pipe instead of MUFU.EX2 (balances the two pipes).
 #ifndef MFA_EMU64
-#define MFA_EMU64 0
+#define MFA_EMU64 1
 #endif
 #ifndef MFA_EMU128
 #define MFA_EMU128 0
@@ -130,17 +141,28 @@ template <int kBias>
 struct DefaultCG {
   static constexpr int value = kBias == 2 ? 2 : kBias == 1 ? MFA_CG_LINEAR : MFA_CG_PLAIN;
 };
+// Tiles per CTA: two 128-row tiles share each K/V block in one CTA, except (MFA_TILES64 = 1)
+// D = 64 with one column group, where one-tile CTAs run two per SM.
+#ifndef MFA_TILES64
+#define MFA_TILES64 1
+#endif
+template <int DP, int CG>
+struct DefaultTiles {
+  static constexpr int value = (DP == 64 && CG == 1) ? MFA_TILES64 : 2;
+};
 __device__ __forceinline__ void named_barrier(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 template <int DP, bool kBF16, int kBias, int CG = DefaultCG<kBias>::value,
-          int kEmu = (DP == 64 ? MFA_EMU64 : MFA_EMU128)>
-__global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
+          int TILES = DefaultTiles<DP, CG>::value,
+          int kEmu = (DP == 64 ? (TILES == 1 ? MFA_EMU64 : 0) : MFA_EMU128)>
+__global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
+                                  sm100::Roles<CG, TILES>::kCtasPerSm)
     fa_fwd_sm100(const __grid_constant__ Sm100Args args) {
   using namespace sm100;
-  using C = Cfg<DP>;
-  using R = Roles<CG>;
+  using C = Cfg<DP, TILES>;
+  using R = Roles<CG, TILES>;
   constexpr int kSoftmaxRegs = R::kSoftmaxRegs;
   constexpr int kOtherRegs = R::kOtherRegs;
   constexpr int NC = R::NC;
@@ -154,7 +176,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* sb = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* sQ = sb;
-  uint8_t* sKV = sb + 2 * C::TILE;
+  uint8_t* sKV = sb + TILES * C::TILE;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sb + C::BAR_OFF);
   uint64_t* q_full = bars;                 // [2]
   uint64_t* kv_full = bars + 2;            // [NSLOT]
@@ -179,10 +201,10 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
   const int b = hb / a.Hq;
   const int hk = h / a.group;
   const SeqView sv = seq_view(a, b);
-  const int r0 = rb * 2 * BM;
+  const int r0 = rb * TILES * BM;
   if (r0 >= sv.lq) return;  // whole CTA leaves before touching barriers or TMEM
 
-  const int r_last = min(r0 + 2 * BM, sv.lq) - 1;
+  const int r_last = min(r0 + TILES * BM, sv.lq) - 1;
   // union of the rows' key intervals: lo and hi are nondecreasing in the row
   int klo = key_range(a, sv, r0).lo;
   int khi = key_range(a, sv, r_last).hi;
@@ -215,7 +237,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
     fence_mbar_init();
   }
   if (warp == R::kMma) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
   if (warp == R::kProducer && lane == 0) {
@@ -236,7 +258,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
     if (n > 0) {
       const int qrow = sv.q0 + r0;
       if (lane == 0) {
-        for (int t = 0; t < 2; ++t) {
+        for (int t = 0; t < TILES; ++t) {
           mbar_expect_tx(&q_full[t], C::TILE);
           for (int c = 0; c < C::NCH; ++c)
             tma_load_4d(sQ + t * C::TILE + c * C::CHUNK, &args.tq, &q_full[t], 64 * c, h,
@@ -287,7 +309,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
       // part run while the softmax is still producing the next one.
       auto pv = [&](int t, int it, bool acc, int j) {
         const uint64_t b0 = dV + (((it % C::NSLOT) * C::TILE) >> 4);
-        const uint32_t d = tmem + 256u + DP * t;
+        const uint32_t d = tmem + C::TMEM_O + DP * t;
         const uint32_t pa = tmem + (C::DECOUPLED ? C::TMEM_P + 64u * t : 128u * t);
 #pragma unroll
         for (int q = 0; q < kPParts; ++q) {
@@ -302,14 +324,16 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
       auto ring_wait = [&](int it) {
         return mbar_wait(&kv_full[it % C::NSLOT], (uint32_t)(it / C::NSLOT) & 1u, abort_flag);
       };
-      bool ok = mbar_wait(&q_full[0], 0, abort_flag) && mbar_wait(&q_full[1], 0, abort_flag) &&
-                ring_wait(0);
+      bool ok = mbar_wait(&q_full[0], 0, abort_flag) &&
+                (TILES == 1 || mbar_wait(&q_full[1], 0, abort_flag)) && ring_wait(0);
       if (ok) {
         tc_fence_after();
         qk(0, 0);
         tc_commit(&s_full[0]);
-        qk(1, 0);
-        tc_commit(&s_full[1]);
+        if constexpr (TILES == 2) {
+          qk(1, 0);
+          tc_commit(&s_full[1]);
+        }
         tc_commit(&kv_empty[0]);
       }
       if constexpr (C::DECOUPLED) {
@@ -324,17 +348,21 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
             tc_fence_after();
             qk(0, itK);
             tc_commit(&s_full[0]);
-            if (!(ok = mbar_wait(&s_free[1], (uint32_t)j & 1u, abort_flag))) break;
-            tc_fence_after();
-            qk(1, itK);
-            tc_commit(&s_full[1]);
+            if constexpr (TILES == 2) {
+              if (!(ok = mbar_wait(&s_free[1], (uint32_t)j & 1u, abort_flag))) break;
+              tc_fence_after();
+              qk(1, itK);
+              tc_commit(&s_full[1]);
+            }
             tc_commit(&kv_empty[itK % C::NSLOT]);
           }
           ok = ring_wait(itV) && pv(0, itV, j > 0, j);
           if (!ok) break;
           tc_commit(&pv_done[0]);
-          if (!(ok = pv(1, itV, j > 0, j))) break;
-          tc_commit(&pv_done[1]);
+          if constexpr (TILES == 2) {
+            if (!(ok = pv(1, itV, j > 0, j))) break;
+            tc_commit(&pv_done[1]);
+          }
           tc_commit(&kv_empty[itV % C::NSLOT]);
         }
       } else {
@@ -377,7 +405,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
     const int64_t row = (int64_t)r0 + t * BM + rt;  // row within the sequence
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
     const uint32_t tS = tmem + lane_base + t * 128;
-    const uint32_t tO = tmem + lane_base + 256 + t * DP;
+    const uint32_t tO = tmem + lane_base + C::TMEM_O + t * DP;
     const KeyRange kr = key_range(a, sv, row);
     // tile-uniform interval extremes for the "block needs no mask" test
     const int tile_lo_max = key_range(a, sv, (int64_t)r0 + t * BM + BM - 1).lo;
@@ -617,7 +645,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG>::kThreads, 1)
   __syncthreads();
   if (warp == R::kMma) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, C::TMEM_COLS);
   }
   if (threadIdx.x == 0 && *abort_flag && a.err != nullptr) atomicExch(a.err, 4 /*MFA_ERR_TIMEOUT*/);
 }

@@ -77,6 +77,10 @@ cudaError_t ensure_smem(K kernel, int dev, int bytes) {
   for (int i = 0; i < nseen; ++i)
     if (seen[i] == (const void*)kernel && seen_dev[i] == dev) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  // all of the SM's unified L1/shared storage as shared memory (two one-tile CTAs per SM)
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
   if (e == cudaSuccess && nseen < 256) {
     seen[nseen] = (const void*)kernel;
     seen_dev[nseen] = dev;
@@ -234,10 +238,23 @@ int make_map(CUtensorMap* m, const void* base, int dtype, int D, int H, int64_t 
   return r == CUDA_SUCCESS ? MFA_OK : MFA_ERR_CUDA;
 }
 
+// Tiles per CTA of the tcgen05 kernel fa_fwd_sm100<DP, *, GEN> (its default template argument).
+template <int DP, int GEN>
+constexpr int sm100_tiles() {
+  return DefaultTiles<DP, DefaultCG<GEN>::value>::value;
+}
+int sm100_tiles_rt(bool wide, int gen) {
+  if (wide) return gen == 2 ? sm100_tiles<128, 2>() : gen == 1 ? sm100_tiles<128, 1>() : sm100_tiles<128, 0>();
+  return gen == 2 ? sm100_tiles<64, 2>() : gen == 1 ? sm100_tiles<64, 1>() : sm100_tiles<64, 0>();
+}
+
 template <int DP, bool BF16, int GEN>
 int launch_sm100(const Sm100Args& args, int dev, int64_t grid, cudaStream_t st) {
   auto k = fa_fwd_sm100<DP, BF16, GEN>;
-  const int smem = (int)sm100::Cfg<DP>::SMEM;
+  constexpr int CG = DefaultCG<GEN>::value;
+  constexpr int TILES = sm100_tiles<DP, GEN>();
+  using R = sm100::Roles<CG, TILES>;
+  const int smem = (int)sm100::Cfg<DP, TILES>::SMEM;
   // The kernel re-splits its registers with setmaxnreg assuming exactly kLaunchRegs per thread
   // at launch; a build that launched with fewer would make setmaxnreg.inc wait forever.
   static int launch_regs = -1;
@@ -246,10 +263,9 @@ int launch_sm100(const Sm100Args& args, int dev, int64_t grid, cudaStream_t st) 
     if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) return MFA_ERR_CUDA;
     launch_regs = fa.numRegs;
   }
-  constexpr int CG = DefaultCG<GEN>::value;
-  if (launch_regs != sm100::Roles<CG>::kLaunchRegs) return MFA_ERR_UNSUPPORTED;
+  if (launch_regs != R::kLaunchRegs) return MFA_ERR_UNSUPPORTED;
   if (ensure_smem(k, dev, smem) != cudaSuccess) return MFA_ERR_CUDA;
-  k<<<(unsigned)grid, sm100::Roles<CG>::kThreads, smem, st>>>(args);
+  k<<<(unsigned)grid, R::kThreads, smem, st>>>(args);
   return MFA_OK;
 }
 
@@ -278,7 +294,10 @@ int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
   if ((rc = make_map(&args.tq, p->q, p->dtype, p->D, p->Hq, Sq, Bm, p->q_stride)) != MFA_OK) return rc;
   if ((rc = make_map(&args.tk, p->k, p->dtype, p->D, p->Hkv, Sk, Bm, p->k_stride)) != MFA_OK) return rc;
   if ((rc = make_map(&args.tv, p->v, p->dtype, p->D, p->Hkv, Sk, Bm, p->v_stride)) != MFA_OK) return rc;
-  a.num_row_blocks = (a.max_lq + 2 * sm100::BM - 1) / (2 * sm100::BM);
+  const int gen = a.softcap > 0.f ? 2 : (!(a.scale > 0.f) || a.alibi != nullptr) ? 1 : 0;
+  const bool wide = p->D > 64;
+  const int rows_per_cta = sm100_tiles_rt(wide, gen) * sm100::BM;
+  a.num_row_blocks = (a.max_lq + rows_per_cta - 1) / rows_per_cta;
   FwdArgs fin = a;  // the caller's output, for the split merge
   fin.num_splits = split.splits;
   float* ws_o = nullptr;
@@ -307,9 +326,7 @@ int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
   const int64_t grid = (int64_t)a.num_row_blocks * a.Hq * a.B * a.num_splits;
   if (grid == 0) return MFA_OK;
   if (grid >= (1ll << 31)) return MFA_ERR_UNSUPPORTED;
-  const int gen = a.softcap > 0.f ? 2 : (!(a.scale > 0.f) || a.alibi != nullptr) ? 1 : 0;
   const bool bf = p->dtype == MFA_BF16;
-  const bool wide = p->D > 64;
 #define MFA_SM100(DP, BF, G)                                                     \
   do {                                                                           \
     const int rc_ = launch_sm100<DP, BF, G>(args, dev, grid, st);                \
