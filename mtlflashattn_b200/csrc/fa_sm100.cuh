@@ -119,18 +119,23 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 //   kBias = 0  x = s                        (c = scale*log2e folded into the exponent)
 //   kBias = 1  x = log2e*(s*scale - slope*|centre - key|)   (any scale, ALiBi optional)
 //   kBias = 2  x = log2e*(softcap(s*scale) - slope*|centre - key|)
-// Column groups per tile; see the role table above. Measured on B200: the softcap and ALiBi
-// paths gain from CG = 2 (ALiBi-only: +17% over CG = 1), the plain path loses 9-17%. Separate
+// Column groups per tile; see the role table above. Measured on B200: the softcap path gains
+// from CG = 2, the plain path loses 9-17%. The ALiBi path (kBias = 1) uses CG = 1 since its
+// bias became two packed FMAs per pair of scores on all but the diagonal blocks (+43% on varlen
+// GQA ALiBi, +55% on dense causal D = 128 ALiBi over CG = 2 with the general bias). Separate
 // kBias = 1 / 2 kernels (rather than one kernel testing softcap at run time) cut the CG = 2
 // register spills and gained 11-13% on the softcap and ALiBi configurations.
 #ifndef MFA_CG_PLAIN
 #define MFA_CG_PLAIN 1
 #endif
 #ifndef MFA_CG_LINEAR
-#define MFA_CG_LINEAR 2
+#define MFA_CG_LINEAR 1
 #endif
 // Softcap: of every 8 pairs of scores, how many take the reciprocal on the FMA pipe (Newton)
 // instead of MUFU.RCP; 2 balances the pipes best on B200 (+1.5% on config 3, 8: -5%).
+#ifndef MFA_ALIBI_LINEAR
+#define MFA_ALIBI_LINEAR 1
+#endif
 #ifndef MFA_RCP_EMU
 #define MFA_RCP_EMU 2
 #endif
@@ -445,7 +450,36 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
       float x[NC];
       const int c0 = (jb + j) * BN + col0;  // local key index of x[0]
       const bool need_mask = ((jb + j) * BN < tile_lo_max) || ((jb + j) * BN + BN > tile_hi_min);
-      if constexpr (kGeneral) {
+      // ALiBi on a block whose keys all lie on one side of the centre of every row of this
+      // warp (every causal block but the diagonal): |centre - key| is linear in the key index,
+      // so the bias is one packed FMA, slope' * i + base, and x = s * scale + bias another.
+      bool linear_bias = false;
+      float lb_slope = 0.f, lb_base = 0.f;
+      if constexpr (kBias == 1 && MFA_ALIBI_LINEAR) {
+        const float kp0 = (float)(c0 + a.k_pos_offset);  // key position of x[0]
+        const float wmin = centre - (float)lane;         // rows of a warp are consecutive
+        const bool left = kp0 + (float)(NC - 1) <= wmin, right = kp0 >= wmin + 31.f;
+        linear_bias = left || right;
+        lb_slope = left ? slope_l2 : -slope_l2;  // bias = -slope |c - k| = lb_slope (k - c)
+        lb_base = lb_slope * (kp0 - centre);
+      }
+      if (kBias == 1 && linear_bias) {
+        const uint64_t sl2 = f2pack(lb_slope, lb_slope), base2 = f2pack(lb_base, lb_base);
+        const uint64_t sc2 = f2pack(pl_scale, pl_scale);
+#pragma unroll
+        for (int i = 0; i < NC; i += 2) {
+          const uint64_t s2 = f2pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+          const uint64_t b2 = ffma2(sl2, f2pack((float)i, (float)(i + 1)), base2);
+          f2unpack(ffma2(s2, sc2, b2), x[i], x[i + 1]);
+        }
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < NC; ++i) {
+            const int kl = c0 + i;
+            if (kl < kr.lo || kl >= kr.hi) x[i] = -INFINITY;
+          }
+        }
+      } else if constexpr (kGeneral) {
         // x = log2(e) * (softcap(s * scale) - slope * |centre - key|)
         const float d0 = centre - (float)(c0 + a.k_pos_offset);  // centre - key for i = 0
 #pragma unroll

@@ -193,6 +193,24 @@ def test_row_max_jumps_in_later_key_blocks(D, dtype, causal):
     check_close(out, want, dtype, f"jumps D={D} {dtype} causal={causal}")
 
 
+@pytest.mark.parametrize("D,dtype", [(64, torch.bfloat16), (128, torch.float16), (96, torch.bfloat16)])
+@pytest.mark.parametrize("Lq,Lk", [(700, 700), (300, 1000), (1000, 300)])
+@pytest.mark.parametrize("causal,window", [(True, (-1, -1)), (False, (-1, -1)),
+                                           (False, (300, 200)), (True, (500, -1))])
+def test_alibi_blocks_on_either_side_of_the_centre(D, dtype, Lq, Lk, causal, window):
+    """ALiBi where key blocks lie left of, right of and across the rows' centres (the kernel
+    uses a linear bias on one-sided blocks and |centre - key| on the others), with bottom-right
+    alignment shifting the centres when Lq != Lk."""
+    q, k, v = ref.make_qkv(1, Lq, Lk, 4, 2, D, dtype, seed=Lq * 3 + Lk + D)
+    slopes = torch.tensor([0.5, 0.05, 0.005, 0.0005])
+    want = ref.flash_attn_func(q, k, v, causal=causal, window_size=window, alibi_slopes=slopes)
+    with pytest.MonkeyPatch.context() as mp:
+        mp.setenv("MTLFLASHATTN_KERNEL", "tcgen05")
+        out = mfa.flash_attn_func(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal,
+                                  window_size=window, alibi_slopes=slopes.to(DEV))
+    check_close(out, want, dtype, f"alibi D={D} Lq={Lq} Lk={Lk} causal={causal} window={window}")
+
+
 def test_empty_and_degenerate_shapes():
     for (B, Lq, Lk) in ((0, 16, 16), (1, 0, 16), (1, 16, 0)):
         q, k, v = ref.make_qkv(max(B, 1), Lq, Lk, 2, 2, 64, torch.bfloat16)
