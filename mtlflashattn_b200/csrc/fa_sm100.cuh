@@ -128,6 +128,9 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 #ifndef MFA_CG_PLAIN
 #define MFA_CG_PLAIN 1
 #endif
+#ifndef MFA_CG_SOFTCAP
+#define MFA_CG_SOFTCAP 2
+#endif
 #ifndef MFA_CG_LINEAR
 #define MFA_CG_LINEAR 1
 #endif
@@ -144,7 +147,7 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 #endif
 template <int kBias>
 struct DefaultCG {
-  static constexpr int value = kBias == 2 ? 2 : kBias == 1 ? MFA_CG_LINEAR : MFA_CG_PLAIN;
+  static constexpr int value = kBias == 2 ? MFA_CG_SOFTCAP : kBias == 1 ? MFA_CG_LINEAR : MFA_CG_PLAIN;
 };
 // Tiles per CTA: two 128-row tiles share each K/V block in one CTA, except (MFA_TILES64 = 1)
 // D = 64 with one column group, where one-tile CTAs run two per SM.
