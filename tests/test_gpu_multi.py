@@ -19,4 +19,4 @@ def test_head_shard_and_split_kv_two_ranks():
                         "--master-port", "29533", os.path.join(HERE, "workers", "mgpu_check.py")],
                        capture_output=True, text=True, timeout=600, env=env)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
-    assert r.stdout.count("head-shard exact") == 2
+    assert r.stdout.count("head-shard ok") == 2
