@@ -76,14 +76,13 @@ struct Cfg {
   static constexpr int NCH = DP / 64;                    // 128-byte column chunks per row
   static constexpr uint32_t CHUNK = 128u * 128u;         // one chunk of 128 rows: 16 KB
   static constexpr uint32_t TILE = NCH * CHUNK;          // Q tile or K / V block
-  static constexpr int NSLOT = DP == 128 ? 3 : TILES == 1 ? 5 : 6;  // K/V ring depth
+  static constexpr int NSLOT = DP == 128 ? (TILES == 1 ? 2 : 3) : TILES == 1 ? 5 : 6;  // K/V ring
   static constexpr uint32_t BAR_OFF = TILES * TILE + NSLOT * TILE;
   static constexpr uint32_t XCH_OFF = BAR_OFF + 256;     // [parity][tile][cg][row] fp32 (CG = 2)
   // TMEM columns: S_t at 128 t, O_t at TMEM_O + DP t, and (decoupled) P_t at TMEM_P + 64 t.
   // D = 64 leaves room for P in its own columns and S is released to the MMA as soon as it is
   // in registers (see "decoupled" below). D = 128 aliases P over S.
   static constexpr bool DECOUPLED = DP == 64;
-  static_assert(TILES == 2 || DECOUPLED, "one-tile CTAs use the decoupled protocol");
   static constexpr uint32_t TMEM_O = 128u * TILES;
   static constexpr uint32_t TMEM_P = 128u * TILES + (uint32_t)DP * TILES;
   static constexpr uint32_t TMEM_COLS = TILES == 1 ? 256 : 512;
@@ -154,9 +153,12 @@ struct DefaultCG {
 #ifndef MFA_TILES64
 #define MFA_TILES64 1
 #endif
+#ifndef MFA_TILES128
+#define MFA_TILES128 2
+#endif
 template <int DP, int CG>
 struct DefaultTiles {
-  static constexpr int value = (DP == 64 && CG == 1) ? MFA_TILES64 : 2;
+  static constexpr int value = CG != 1 ? 2 : DP == 64 ? MFA_TILES64 : MFA_TILES128;
 };
 __device__ __forceinline__ void named_barrier(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
@@ -386,12 +388,16 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
           qk(0, itK);
           tc_commit(&s_full[0]);
         }
-        if (!(ok = pv(1, itV, j > 0, j))) break;
+        if constexpr (TILES == 2) {
+          if (!(ok = pv(1, itV, j > 0, j))) break;
+        }
         tc_commit(&kv_empty[itV % C::NSLOT]);
-        if (!more) tc_commit(&o_full[1]);
+        if (TILES == 2 && !more) tc_commit(&o_full[1]);
         if (more) {
-          qk(1, itK);
-          tc_commit(&s_full[1]);
+          if constexpr (TILES == 2) {
+            qk(1, itK);
+            tc_commit(&s_full[1]);
+          }
           tc_commit(&kv_empty[itK % C::NSLOT]);
         }
       }
