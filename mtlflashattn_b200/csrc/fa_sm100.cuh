@@ -2,33 +2,38 @@
 // accumulators -> fp32 online softmax in registers -> P -> P.V on tcgen05.
 //
 // One CTA owns 256 query rows of one (batch, head) as two 128-row tiles (t = 0, 1) and streams
-// the key/value blocks (128 keys each) that any of those rows may attend. For D = 64 without
-// softcap / ALiBi a CTA owns one 128-row tile (TILES = 1) and two CTAs share each SM: their
-// MMA warps issue independently, so the two tiles' softmax phases do not run in lock-step
-// (+1.4% on B=1 H=16 L=8192 causal, +2.7% with 1 of 8 exponential pairs on the FMA pipe).
+// the key/value blocks (128 keys each) that any of those rows may attend. For D = 64 with one
+// column group (no softcap) a CTA owns one 128-row tile (TILES = 1) and two CTAs share each
+// SM: their MMA warps issue independently, so the two tiles' softmax phases do not run in
+// lock-step (+1.4% on B=1 H=16 L=8192 causal, +2.7% with 1 of 8 exponential pairs on the FMA
+// pipe).
 //
-//   warpgroups 0 .. 2*CG-1   softmax: tile t = wg / CG, key columns [cg*128/CG, (cg+1)*128/CG)
-//                            with cg = wg % CG (TMEM lanes 0-127, one query row per thread)
-//   warp 8*CG                TMA producer: Q tiles once, then K_j, V_j into a ring of NSLOT
-//   warp 8*CG+1              TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 8*CG+2, 8*CG+3     idle (they complete the last warpgroup)
+//   warpgroups 0 .. TILES*CG-1   softmax: tile t = wg / CG, key columns [cg*128/CG,
+//                                (cg+1)*128/CG) with cg = wg % CG (TMEM lanes 0-127, one
+//                                query row per thread)
+//   warp W = 4*CG*TILES          TMA producer: Q tiles once, then K_j, V_j into a ring of NSLOT
+//   warp W+1                     TMEM allocator + single-thread tcgen05.mma issuer
+//   warps W+2, W+3               idle (they complete the last warpgroup)
 // With CG = 2 each row's 128 scores are split over two threads in two warpgroups that exchange
 // their partial row maxima (and, at the end, row sums) through shared memory behind a named
 // barrier: twice the softmax warps per SM sub-partition to hide the TMEM / MUFU latencies.
 // Registers: the softmax warpgroups raise theirs and the producer/MMA warpgroup lowers its
-// with setmaxnreg (Roles<CG> below), so each softmax thread keeps its share of a row of S in
-// registers without spilling.
+// with setmaxnreg (Roles<CG, TILES> below), so each softmax thread keeps its share of a row of
+// S in registers without spilling.
 //
-// TMEM columns (512 allocated): S0 [0,128) S1 [128,256) O0 [256,256+DP) O1 [256+DP,256+2DP).
-// P_t (16-bit, two per column) overwrites the first 64 columns of S_t once S_t is in registers.
+// TMEM columns (512 allocated with two tiles, 256 with one): S_t at [128t, 128t+128), O_t
+// after all S tiles, and at D = 64 P_t in its own 64 columns after all O tiles (Cfg below).
+// At D = 128, P_t (16-bit, two per column) overwrites the first 64 columns of S_t once S_t is in
+// registers.
 // The MMA warp issues, per key block j:  PV0_j, S0_{j+1}, PV1_j, S1_{j+1}.  tcgen05 MMAs of
 // one thread execute in issue order, so S_t(j+1) never overwrites P_t(j) before PV_t(j) read it,
 // and the commit that publishes S_t(j+1) also covers PV_t(j); that is what lets the softmax
 // warps rescale O_t in place right after they see S_t(j+1). With CG = 1 the softmax publishes P_t in
 // two key halves on separate mbarriers and the MMA warp issues the first four P.V MMAs while
-// the second half is still being computed (measured +5% on the plain path; quarters: +1-3%). (A variant that released S_t to the
-// MMA as soon as it was in registers, with P in separate TMEM columns or shared memory and an
-// event-driven issuer, measured 5-20% slower on every BASELINE configuration.)
+// the second half is still being computed (measured +5% on the plain path; quarters: +1-3%).
+// (At D = 128, a variant that released S_t to the MMA as soon as it was in registers, with P
+// in shared memory and an event-driven issuer, measured 5-20% slower on every BASELINE
+// configuration.)
 //
 // Semantics follow the reference's chunked-fp32 tier (metal_flash_attn/_kernel.py:1165-1208):
 // scale, softcap, ALiBi, bottom-right causal and sliding window, fully masked rows -> 0.
@@ -107,7 +112,8 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 }  // namespace sm100
 
 // kEmu: of every 8 pairs of probabilities, how many are computed with exp2_poly2 on the FMA
-// pipe instead of MUFU.EX2 (balances the two pipes).
+// pipe instead of MUFU.EX2 (balances the two pipes). Used by one-tile D = 64 CTAs only; at
+// D = 128 and in two-tile CTAs it measured no gain.
 #ifndef MFA_EMU64
 #define MFA_EMU64 1
 #endif
@@ -133,11 +139,12 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 #ifndef MFA_CG_LINEAR
 #define MFA_CG_LINEAR 1
 #endif
-// Softcap: of every 8 pairs of scores, how many take the reciprocal on the FMA pipe (Newton)
-// instead of MUFU.RCP; 2 balances the pipes best on B200 (+1.5% on config 3, 8: -5%).
+// ALiBi kernel: bias as two packed FMAs on key blocks that lie on one side of the rows' centres.
 #ifndef MFA_ALIBI_LINEAR
 #define MFA_ALIBI_LINEAR 1
 #endif
+// Softcap: of every 8 pairs of scores, how many take the reciprocal on the FMA pipe (Newton)
+// instead of MUFU.RCP; 2 balances the pipes best on B200 (+1.5% on config 3, 8: -5%).
 #ifndef MFA_RCP_EMU
 #define MFA_RCP_EMU 2
 #endif
@@ -149,7 +156,8 @@ struct DefaultCG {
   static constexpr int value = kBias == 2 ? MFA_CG_SOFTCAP : kBias == 1 ? MFA_CG_LINEAR : MFA_CG_PLAIN;
 };
 // Tiles per CTA: two 128-row tiles share each K/V block in one CTA, except (MFA_TILES64 = 1)
-// D = 64 with one column group, where one-tile CTAs run two per SM.
+// D = 64 with one column group, where one-tile CTAs run two per SM. MFA_TILES128 = 1 does the
+// same at D = 128 (measured slower: every K/V block is fetched by two CTAs).
 #ifndef MFA_TILES64
 #define MFA_TILES64 1
 #endif
