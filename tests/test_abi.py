@@ -88,3 +88,14 @@ def test_wait_selftest_argument_checks():
     lib = _lib.load()
     assert lib.mfa_selftest_wait_timeout(None, 1000, None) == _lib.ERR_INVALID
     assert lib.mfa_selftest_wait_timeout(None, 0, None) == _lib.ERR_INVALID
+
+
+def test_staged_entry_checks_before_any_cuda_call(monkeypatch):
+    lib = _lib.load()
+    p = _lib.MfaFwdParams()
+    io = _lib.MfaHostIo()
+    assert lib.mfa_fwd_staged(ctypes.byref(p), None, None) == _lib.ERR_INVALID
+    p.D, p.Hq, p.Hkv, p.dtype, p.o_dtype = 160, 1, 1, _lib.BF16, -1
+    assert lib.mfa_fwd_staged(ctypes.byref(p), ctypes.byref(io), None) == _lib.ERR_UNSUPPORTED
+    monkeypatch.setenv("MFA_FAULT", "fwd")
+    assert lib.mfa_fwd_staged(ctypes.byref(p), ctypes.byref(io), None) == _lib.ERR_FAULT_INJECTED
