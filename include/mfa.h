@@ -143,8 +143,8 @@ typedef struct {
   void* o;               /* output in host memory, same strides as p->o */
   const int32_t* cu_q;   /* varlen only: host copies of p->cu_q / p->cu_k ([B + 1]) */
   const int32_t* cu_k;
-  int32_t chunks;        /* pipeline pieces: 0 = automatic (each piece at least one wave of
-                            256-row CTAs, at most 16), 1 = copy, compute, copy back */
+  int32_t chunks;        /* pipeline pieces: 0 = automatic (about half a wave of 256-row
+                            CTAs per piece, at most 16), 1 = copy, compute, copy back */
 } mfa_host_io;
 
 /* Forward of host-resident inputs into a host-resident output (no counterpart in the
