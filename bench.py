@@ -5,9 +5,11 @@
 
 One step = one forward of the workload over inputs already resident in HBM (``value``), and,
 separately, the same workload through the public host-memory API (``flash_attn_host``) with
-pinned host inputs copied in and the output copied back inside the timed region (``e2e``). The default workload is BASELINE config
-2 (B=1, H=16, L=8192, D=64, bf16, causal). With N ranks each rank runs its own instance
-(batch-sharded, no collective: weak scaling); the reported time is the max over ranks.
+pinned host inputs copied in and the output copied back inside the timed region (``e2e``).
+The default workload is BASELINE config 2 (B=1, H=16, L=8192, D=64, bf16, causal). With N ranks
+each rank runs its own instance (batch-sharded, no collective: weak scaling), except config 5
+(one 131072-token sequence), whose heads are sharded over the ranks (strong scaling); the
+reported time is the max over ranks.
 
 ``--impl reference`` times the reference's own CPU algorithm (the chunked-fp32 torch tier,
 restated in oracle/flash_torch.py) on the host cores, on a bounded sample of the same workload.
@@ -45,7 +47,7 @@ def peaks():
 
 
 # ------------------------------------------------------------------------------ workloads
-def workload(cfg, device, rank=0):
+def workload(cfg, device, rank=0, world=1):
     """Synthetic inputs with the BASELINE config's shapes and distributions (N(0,1), seeded).
     Returns (call(q, k, v) launching exactly one kernel, host inputs, algorithmic FLOPs,
     compulsory HBM bytes, description)."""
@@ -63,11 +65,20 @@ def workload(cfg, device, rank=0):
         else:
             B, L, H, D, dt, causal, kw = 1, 131072, 16, 128, torch.bfloat16, True, {}
         sc = 0.5 if cfg == "5" else 1.0
-        q = (torch.randn(B, L, H, D, generator=g) * sc).to(dt)
-        k = (torch.randn(B, L, H, D, generator=g) * sc).to(dt)
-        v = (torch.randn(B, L, H, D, generator=g) * sc).to(dt)
-        flops = attention_flops(B, H, L, L, D, causal, kw.get("window_size", (-1, -1)))
-        nbytes = compulsory_bytes(B, H, H, L, L, D)
+        # config 5 on N ranks: one sequence, head-sharded (each rank its KV-group-aligned heads,
+        # no communication): strong scaling of the whole problem
+        strong = cfg == "5" and world > 1
+        Hr = H
+        if strong:
+            from mtlflashattn_b200.distributed import head_shard
+
+            h0, h1 = head_shard(H, H, world, rank)
+            Hr = h1 - h0
+        q = (torch.randn(B, L, Hr, D, generator=g) * sc).to(dt)
+        k = (torch.randn(B, L, Hr, D, generator=g) * sc).to(dt)
+        v = (torch.randn(B, L, Hr, D, generator=g) * sc).to(dt)
+        flops = attention_flops(B, Hr, L, L, D, causal, kw.get("window_size", (-1, -1)))
+        nbytes = compulsory_bytes(B, Hr, Hr, L, L, D)
 
         def call(q, k, v):
             return mfa.flash_attn_func(q, k, v, causal=causal, **kw)
@@ -82,6 +93,9 @@ def workload(cfg, device, rank=0):
                     seq_len=L, heads=H, head_dim=D, dtype=str(dt).replace("torch.", ""),
                     causal=causal, **{k_: list(v_) if isinstance(v_, tuple) else v_
                                       for k_, v_ in kw.items()})
+        if strong:
+            desc.update(heads_per_rank=Hr, strong=True,
+                        total_flops=attention_flops(B, H, L, L, D, causal, (-1, -1)))
         return call, (q, k, v), flops, nbytes, desc
     if cfg == "4":
         lens = torch.randint(256, 8193, (16,), generator=torch.Generator().manual_seed(0)).tolist()
@@ -270,7 +284,9 @@ def run_gpu(args):
         if dist is not None:
             dist.barrier()
 
-    call, host_in, flops, nbytes, desc = workload(args.config, dev, rank)
+    call, host_in, flops, nbytes, desc = workload(args.config, dev, rank, world)
+    strong = bool(desc.pop("strong", False))
+    total_flops = desc.pop("total_flops", world * flops)
     dev_in = [t.to(dev) for t in host_in]
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -291,7 +307,7 @@ def run_gpu(args):
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_step = t.item() / args.steps
-    value = world * flops / (ms_step * 1e-3) / 1e12
+    value = total_flops / (ms_step * 1e-3) / 1e12
 
     # end-to-end through the public host-memory API (flash_attn_host): pinned host inputs in,
     # the output back in pinned host memory; the library overlaps the copies with the compute
@@ -329,12 +345,16 @@ def run_gpu(args):
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if strong else "weak",
+            "vs_baseline": None,
             "dtype": desc.get("dtype", "bfloat16").replace("bfloat16", "bf16").replace(
                 "float16", "fp16"),
             "data": "synthetic (seeded N(0,1), BASELINE shapes)",
-            "config": dict(desc, global_batch=world * desc.get("batch_per_rank", 1),
-                           parallelism=f"dp{world} (batch shards, no collective)",
+            "config": dict(desc, global_batch=(desc.get("batch_per_rank", 1) if strong else
+                                              world * desc.get("batch_per_rank", 1)),
+                           parallelism=(f"heads{world} (one sequence, KV-group-aligned head "
+                                        "shards, no collective)" if strong else
+                                        f"dp{world} (batch shards, no collective)"),
                            l2="flushed (256 MiB write) before every timed step"),
             "pct_of_peak": round(100 * value / world / pk["bf16"], 2),
             "hbm_gbs_compulsory": round(nbytes / (ms_step * 1e-3) / 1e9, 1),
@@ -343,7 +363,7 @@ def run_gpu(args):
                          "frac": round(achieved / pk["bf16"], 4),
                          "peak_source": f"bf16_tflops (burst) of {pk['source']} peaks",
                          "traffic": traffic},
-            "e2e": {"value": round(world * flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+            "e2e": {"value": round(total_flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms, 4),
                     "api": "flash_attn_host / flash_attn_varlen_host (host tensors in and out; "
