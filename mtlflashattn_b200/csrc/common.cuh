@@ -33,6 +33,10 @@ struct FwdArgs {
   int lk_total;  // 0 = per-sequence Lk
   int* err;
   int num_row_blocks;  // row blocks per (batch, head) for this launch's kernel
+  // CTA order: (batch, head) pairs in groups of group_hb (whole KV groups, sized so one group's
+  // K/V fits comfortably in L2), groups one after the other, heaviest row blocks first within
+  // a group; group_hb = B * Hq is one group (plain heaviest-first order)
+  int group_hb;
   // key split within one launch (1 = none): CTA (row block, batch, head, split) covers the local
   // keys [split * split_keys, (split + 1) * split_keys) and writes its partial output at
   // o + split * o_split_stride and its row log-sum-exp at lse + split * lse_split_stride

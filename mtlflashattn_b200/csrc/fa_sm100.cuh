@@ -210,11 +210,16 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
   float* xch = reinterpret_cast<float*>(sb + C::XCH_OFF);
 
   // ---- work decode: heaviest row blocks first across all (batch, head)
-  const int HBS = a.Hq * a.B * a.num_splits;
+  // (groups of (batch, head) pairs whose K/V fits in L2, one after the other)
   const int idx = blockIdx.x;
-  const int rb = a.num_row_blocks - 1 - idx / HBS;
-  const int split = (idx % HBS) % a.num_splits;  // splits of one row block run side by side
-  const int hb = (idx % HBS) / a.num_splits;
+  const int per_group = a.num_row_blocks * a.group_hb * a.num_splits;
+  const int grp = idx / per_group;
+  const int hb0 = grp * a.group_hb;
+  const int GHS = min(a.group_hb, a.Hq * a.B - hb0) * a.num_splits;  // CTAs per row block
+  const int ri = idx - grp * per_group;
+  const int rb = a.num_row_blocks - 1 - ri / GHS;
+  const int split = (ri % GHS) % a.num_splits;  // splits of one row block run side by side
+  const int hb = hb0 + (ri % GHS) / a.num_splits;
   const int h = hb % a.Hq;
   const int b = hb / a.Hq;
   const int hk = h / a.group;

@@ -298,6 +298,16 @@ int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
   const bool wide = p->D > 64;
   const int rows_per_cta = sm100_tiles_rt(wide, gen) * sm100::BM;
   a.num_row_blocks = (a.max_lq + rows_per_cta - 1) / rows_per_cta;
+  {
+    // K/V bytes of one KV head of one sequence; groups of whole KV groups whose K/V stays
+    // within ~64 MB of L2 (all of them when everything fits)
+    const int64_t kv_unit = (int64_t)(varlen ? p->max_lk : p->Lk) * p->D * 2 * 2;
+    int64_t units = kv_unit > 0 ? (64ll << 20) / kv_unit : (1ll << 30);
+    if (units < 1) units = 1;
+    const int64_t all = (int64_t)p->Hq * a.B;
+    const int64_t ghb = units * (p->Hq / p->Hkv);
+    a.group_hb = (int)(ghb < all ? ghb : all);
+  }
   FwdArgs fin = a;  // the caller's output, for the split merge
   fin.num_splits = split.splits;
   float* ws_o = nullptr;

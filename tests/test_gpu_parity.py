@@ -122,6 +122,16 @@ def test_baseline_config_dense(cfg):
     check_close(out, want, q.dtype, f"config {cfg}")
 
 
+def test_baseline_config1_cpu_case():
+    """BASELINE config 1, the reference's CPU-runnable case: B=1, H=4, L=1024, D=64, fp32
+    N(0,1) from seed 0, non-causal, scale 1/8, against the CPU oracle at the fp32 bar."""
+    q, k, v = ref.make_qkv(1, 1024, 1024, 4, 4, 64, torch.float32, seed=0)
+    out = mfa.flash_attn_func(q.to(DEV), k.to(DEV), v.to(DEV), softmax_scale=0.125)
+    want = ref.flash_attn_func(q, k, v, softmax_scale=0.125)
+    bar_check(out.cpu(), want, torch.float32, "config 1")
+    check_close(out, want, torch.float32, "config 1")
+
+
 def test_baseline_config4_varlen_gqa_alibi():
     lens = torch.randint(256, 8193, (16,), generator=torch.Generator().manual_seed(0)).tolist()
     q, k, v, cu_q, cu_k = ref.make_varlen(lens, lens, 32, 8, 128, torch.bfloat16, seed=1)
