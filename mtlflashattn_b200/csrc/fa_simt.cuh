@@ -196,14 +196,33 @@ __global__ void lse_combine_kernel(const __grid_constant__ PartPtrs pp, int n, i
 
 // Merge of the key splits of one launch (dense layout): partial outputs ws_o fp32
 // [split][B][Lq][Hq][D] normalised by their own sums, row log-sum-exp ws_lse [split][B][Hq][Lq].
-// One warp per (batch, head, row); writes the final row in the caller's dtype and strides.
+// One block of kCombineThreads per (batch, head, row): the split weights exp(lse_s - max) are
+// computed in parallel into shared memory (a.num_splits floats of dynamic shared memory), then
+// each thread sums its output columns over the splits with independent loads; the final row is
+// written in the caller's dtype and strides.
+constexpr int kCombineThreads = 128;
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // red may still be read by the previous reduction
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  v = red[0];
+  for (int w = 1; w < kCombineThreads / 32; ++w) v = is_max ? fmaxf(v, red[w]) : v + red[w];
+  return v;
+}
+
 template <typename TO>
-__global__ void split_combine_kernel(const FwdArgs a, const float* __restrict__ ws_o,
-                                     const float* __restrict__ ws_lse, TO* o, float* lse_out) {
-  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  const int64_t rows = (int64_t)a.B * a.Hq * a.Lq;
-  if (w >= rows) return;
+__global__ void __launch_bounds__(kCombineThreads)
+    split_combine_kernel(const FwdArgs a, const float* __restrict__ ws_o,
+                         const float* __restrict__ ws_lse, TO* o, float* lse_out) {
+  extern __shared__ float sw[];  // [num_splits]
+  __shared__ float red[kCombineThreads / 32];
+  const int64_t w = blockIdx.x;
   const int row = (int)(w % a.Lq);
   const int bh = (int)(w / a.Lq);
   const int h = bh % a.Hq, b = bh / a.Hq;
@@ -211,27 +230,34 @@ __global__ void split_combine_kernel(const FwdArgs a, const float* __restrict__ 
   const int64_t lstride = (int64_t)a.B * a.Hq * a.Lq;
   const int64_t ostride = lstride * a.D;
   const int64_t oi = (((int64_t)b * a.Lq + row) * a.Hq + h) * a.D;
+  const int S = a.num_splits;
   float mx = -INFINITY;
-  for (int s = 0; s < a.num_splits; ++s) mx = fmaxf(mx, ws_lse[s * lstride + li]);
+  for (int s = threadIdx.x; s < S; s += kCombineThreads) mx = fmaxf(mx, ws_lse[s * lstride + li]);
+  mx = block_reduce(mx, true, red);
   float tot = 0.f;
-  if (mx != -INFINITY)
-    for (int s = 0; s < a.num_splits; ++s) tot += expf(ws_lse[s * lstride + li] - mx);
-  const float lse = mx == -INFINITY ? -INFINITY : mx + logf(tot);
+  for (int s = threadIdx.x; s < S; s += kCombineThreads) {
+    const float ls = ws_lse[s * lstride + li];
+    const float e = (mx == -INFINITY || ls == -INFINITY) ? 0.f : expf(ls - mx);
+    sw[s] = e;
+    tot += e;
+  }
+  tot = block_reduce(tot, false, red);  // its barriers also publish sw
+  const float inv = tot > 0.f ? 1.f / tot : 0.f;
   TO* orow = o + (int64_t)b * a.o_sb + (int64_t)row * a.o_ss + (int64_t)h * a.o_sh;
-  for (int d = lane; d < a.D; d += 32) {
+  for (int d = threadIdx.x; d < a.D; d += kCombineThreads) {
     float acc = 0.f;
-    if (lse != -INFINITY)
-      for (int s = 0; s < a.num_splits; ++s) {
-        const float ls = ws_lse[s * lstride + li];
-        if (ls != -INFINITY) acc = fmaf(expf(ls - lse), ws_o[s * ostride + oi + d], acc);
-      }
+#pragma unroll 8
+    for (int s = 0; s < S; ++s) acc = fmaf(sw[s], ws_o[s * ostride + oi + d], acc);
+    acc *= inv;
     if constexpr (sizeof(TO) == 4) {
       orow[d] = acc;
     } else {
       orow[d] = TO(acc);
     }
   }
-  if (lane == 0 && lse_out != nullptr) lse_out[(int64_t)b * a.lse_sb + (int64_t)h * a.lse_sh + row] = lse;
+  if (threadIdx.x == 0 && lse_out != nullptr)
+    lse_out[(int64_t)b * a.lse_sb + (int64_t)h * a.lse_sh + row] =
+        tot > 0.f ? mx + logf(tot) : -INFINITY;
 }
 
 // Self-test of the bounded wait every pipelined kernel uses: one thread waits on an mbarrier

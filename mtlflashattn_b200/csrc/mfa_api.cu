@@ -271,14 +271,17 @@ int launch_sm100(const Sm100Args& args, int dev, int64_t grid, cudaStream_t st) 
 
 int launch_combine(const FwdArgs& fin, const float* ws_o, const float* ws_lse, void* o,
                    float* lse, cudaStream_t st) {
-  const int64_t warps = (int64_t)fin.B * fin.Hq * fin.Lq;
-  const unsigned blocks = (unsigned)((warps * 32 + 255) / 256);
+  const int64_t rows = (int64_t)fin.B * fin.Hq * fin.Lq;
+  if (rows == 0) return MFA_OK;
+  if (rows >= (1ll << 31)) return MFA_ERR_UNSUPPORTED;
+  const unsigned blocks = (unsigned)rows;
+  const int smem = fin.num_splits * (int)sizeof(float);
   if (fin.o_dtype == MFA_FP32)
-    split_combine_kernel<float><<<blocks, 256, 0, st>>>(fin, ws_o, ws_lse, (float*)o, lse);
+    split_combine_kernel<float><<<blocks, kCombineThreads, smem, st>>>(fin, ws_o, ws_lse, (float*)o, lse);
   else if (fin.o_dtype == MFA_BF16)
-    split_combine_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(fin, ws_o, ws_lse, (__nv_bfloat16*)o, lse);
+    split_combine_kernel<__nv_bfloat16><<<blocks, kCombineThreads, smem, st>>>(fin, ws_o, ws_lse, (__nv_bfloat16*)o, lse);
   else
-    split_combine_kernel<__half><<<blocks, 256, 0, st>>>(fin, ws_o, ws_lse, (__half*)o, lse);
+    split_combine_kernel<__half><<<blocks, kCombineThreads, smem, st>>>(fin, ws_o, ws_lse, (__half*)o, lse);
   return MFA_OK;
 }
 
