@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define MFA_ABI_VERSION 3
+#define MFA_ABI_VERSION 4
 
 /* Status codes. The Python layer maps them to the reference's exception types. */
 enum mfa_status {
@@ -121,6 +121,12 @@ size_t mfa_fwd_workspace_size(const mfa_fwd_params* p);
 /* Number of key splits mfa_fwd would use for these params with the workspace they carry (1 =
  * no split), or a negative mfa_status. Lets callers and tests see the plan. */
 int mfa_fwd_num_splits(const mfa_fwd_params* p);
+
+/* Query heads mfa_fwd packs into the rows of one tile per KV head for these params (1 = none),
+ * or a negative mfa_status. Decode-like GQA/MQA calls (fewer than 128 query rows per sequence,
+ * a power-of-two group of at most 16) load each K/V block once per KV group instead of once per
+ * query head. No counterpart in the reference, which runs one threadgroup row per query head. */
+int mfa_fwd_packed_heads(const mfa_fwd_params* p);
 
 /* Which kernel mfa_fwd would run for these params (mfa_kernel value, never AUTO), or a
  * negative mfa_status if the call would be rejected. Replaces the label logic of the

@@ -13,7 +13,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmfa.so")
 
-MFA_ABI_VERSION = 3
+MFA_ABI_VERSION = 4
 
 # mfa_status
 OK = 0
@@ -39,6 +39,7 @@ EXPORTED_SYMBOLS = (
     "mfa_fwd_staged",
     "mfa_fwd_workspace_size",
     "mfa_fwd_num_splits",
+    "mfa_fwd_packed_heads",
     "mfa_select_kernel",
     "mfa_lse_combine",
     "mfa_selftest_wait_timeout",
@@ -140,6 +141,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
         lib.mfa_fwd_workspace_size.restype = ctypes.c_size_t
         lib.mfa_fwd_num_splits.argtypes = [ctypes.POINTER(MfaFwdParams)]
         lib.mfa_fwd_num_splits.restype = ctypes.c_int
+        lib.mfa_fwd_packed_heads.argtypes = [ctypes.POINTER(MfaFwdParams)]
+        lib.mfa_fwd_packed_heads.restype = ctypes.c_int
         lib.mfa_select_kernel.argtypes = [ctypes.POINTER(MfaFwdParams)]
         lib.mfa_select_kernel.restype = ctypes.c_int
         lib.mfa_lse_combine.argtypes = [
@@ -187,6 +190,10 @@ def workspace_size(params: MfaFwdParams) -> int:
 
 def num_splits(params: MfaFwdParams) -> int:
     return load().mfa_fwd_num_splits(ctypes.byref(params))
+
+
+def packed_heads(params: MfaFwdParams) -> int:
+    return load().mfa_fwd_packed_heads(ctypes.byref(params))
 
 
 def select_kernel(params: MfaFwdParams) -> int:

@@ -44,6 +44,11 @@ struct FwdArgs {
   int split_keys;
   int64_t o_split_stride;
   int64_t lse_split_stride;
+  // query heads packed per KV head (tcgen05 kernel only): 0 = off, else a CTA serves one
+  // (batch, KV head) and its tile row r is query position r >> pack_shift of query head
+  // hk * 2^pack_shift + (r & (2^pack_shift - 1)); the 2^pack_shift heads of a KV group share
+  // every K/V block load
+  int pack_shift;
 };
 
 // One (batch, sequence) view after resolving dense vs varlen.

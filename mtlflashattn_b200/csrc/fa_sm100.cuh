@@ -47,6 +47,8 @@ namespace mfa {
 
 struct Sm100Args {
   CUtensorMap tq, tk, tv;  // 4-D maps (D, H, S, B), box (64, 1, 128, 1), 128B swizzle
+  // head-packed query map: box (64, 2^pack_shift, 128 >> pack_shift, 1), rows head-fastest
+  CUtensorMap tqp;
   FwdArgs a;
 };
 
@@ -140,6 +142,9 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 #define MFA_CG_LINEAR 1
 #endif
 // ALiBi kernel: bias as two packed FMAs on key blocks that lie on one side of the rows' centres.
+#ifndef MFA_PACK_GQA
+#define MFA_PACK_GQA 1  // pack the query heads of a KV group into tile rows on decode shapes
+#endif
 #ifndef MFA_ALIBI_LINEAR
 #define MFA_ALIBI_LINEAR 1
 #endif
@@ -168,12 +173,18 @@ template <int DP, int CG>
 struct DefaultTiles {
   static constexpr int value = CG != 1 ? 2 : DP == 64 ? MFA_TILES64 : MFA_TILES128;
 };
+template <bool B>
+struct BoolC {
+  static constexpr bool value = B;
+};
 __device__ __forceinline__ void named_barrier(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// kPack: the row mapping of decode-like launches (query heads packed per KV head, one-tile CTAs);
+// the other instantiations fold pack_shift to 0 at compile time.
 template <int DP, bool kBF16, int kBias, int CG = DefaultCG<kBias>::value,
-          int TILES = DefaultTiles<DP, CG>::value,
+          int TILES = DefaultTiles<DP, CG>::value, bool kPack = false,
           int kEmu = (DP == 64 ? (TILES == 1 ? MFA_EMU64 : 0) : MFA_EMU128)>
 __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
                                   sm100::Roles<CG, TILES>::kCtasPerSm)
@@ -215,22 +226,30 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
   const int per_group = a.num_row_blocks * a.group_hb * a.num_splits;
   const int grp = idx / per_group;
   const int hb0 = grp * a.group_hb;
-  const int GHS = min(a.group_hb, a.Hq * a.B - hb0) * a.num_splits;  // CTAs per row block
+  // head-packed: one CTA per (batch, KV head); tile row r is position r >> ps of query head
+  // (hk << ps) + (r & pmask). Unpacked (ps = 0): one CTA per (batch, query head), r = position.
+  const int ps = kPack ? a.pack_shift : 0;
+  const int pmask = (1 << ps) - 1;
+  const int heads = a.Hq >> ps;
+  const int GHS = min(a.group_hb, heads * a.B - hb0) * a.num_splits;  // CTAs per row block
   const int ri = idx - grp * per_group;
   const int rb = a.num_row_blocks - 1 - ri / GHS;
   const int split = (ri % GHS) % a.num_splits;  // splits of one row block run side by side
   const int hb = hb0 + (ri % GHS) / a.num_splits;
-  const int h = hb % a.Hq;
-  const int b = hb / a.Hq;
-  const int hk = h / a.group;
+  const int hu = hb % heads;  // query head, or KV head when packed
+  const int b = hb / heads;
+  const int hk = ps ? hu : hu / a.group;
   const SeqView sv = seq_view(a, b);
+  const int rows = sv.lq << ps;  // tile rows of this (batch, head unit)
   const int r0 = rb * TILES * BM;
-  if (r0 >= sv.lq) return;  // whole CTA leaves before touching barriers or TMEM
+  if (r0 >= rows) return;  // whole CTA leaves before touching barriers or TMEM
+  // tiles holding at least one row (a last row block may leave the second tile empty)
+  const int nt = (TILES == 2 && r0 + BM < rows) ? 2 : 1;
 
-  const int r_last = min(r0 + TILES * BM, sv.lq) - 1;
-  // union of the rows' key intervals: lo and hi are nondecreasing in the row
-  int klo = key_range(a, sv, r0).lo;
-  int khi = key_range(a, sv, r_last).hi;
+  const int r_last = min(r0 + TILES * BM, rows) - 1;
+  // union of the rows' key intervals: lo and hi are nondecreasing in the position
+  int klo = key_range(a, sv, r0 >> ps).lo;
+  int khi = key_range(a, sv, r_last >> ps).hi;
   if (a.num_splits > 1) {
     klo = max(klo, split * a.split_keys);
     khi = min(khi, (split + 1) * a.split_keys);
@@ -264,7 +283,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
     tmem_relinquish();
   }
   if (warp == R::kProducer && lane == 0) {
-    tma_prefetch_map(&args.tq);
+    tma_prefetch_map(ps ? &args.tqp : &args.tq);
     tma_prefetch_map(&args.tk);
     tma_prefetch_map(&args.tv);
   }
@@ -279,13 +298,18 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
     regs_dec<kOtherRegs>();
     // ------------------------------------------------------------ TMA producer
     if (n > 0) {
-      const int qrow = sv.q0 + r0;
       if (lane == 0) {
-        for (int t = 0; t < TILES; ++t) {
+        for (int t = 0; t < nt; ++t) {
           mbar_expect_tx(&q_full[t], C::TILE);
-          for (int c = 0; c < C::NCH; ++c)
-            tma_load_4d(sQ + t * C::TILE + c * C::CHUNK, &args.tq, &q_full[t], 64 * c, h,
-                        qrow + t * BM, sv.qb);
+          const int qpos = sv.q0 + ((r0 + t * BM) >> ps);
+          for (int c = 0; c < C::NCH; ++c) {
+            if (ps)
+              tma_load_4d(sQ + t * C::TILE + c * C::CHUNK, &args.tqp, &q_full[t], 64 * c, hk << ps,
+                          qpos, sv.qb);
+            else
+              tma_load_4d(sQ + t * C::TILE + c * C::CHUNK, &args.tq, &q_full[t], 64 * c, hu, qpos,
+                          sv.qb);
+          }
         }
       }
       for (int it = 0; it < 2 * n; ++it) {
@@ -347,73 +371,83 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
       auto ring_wait = [&](int it) {
         return mbar_wait(&kv_full[it % C::NSLOT], (uint32_t)(it / C::NSLOT) & 1u, abort_flag);
       };
-      bool ok = mbar_wait(&q_full[0], 0, abort_flag) &&
-                (TILES == 1 || mbar_wait(&q_full[1], 0, abort_flag)) && ring_wait(0);
-      if (ok) {
-        tc_fence_after();
-        qk(0, 0);
-        tc_commit(&s_full[0]);
-        if constexpr (TILES == 2) {
-          qk(1, 0);
-          tc_commit(&s_full[1]);
+      // The issue loop is compiled for one and for two active tiles (a last row block may
+      // leave the second tile empty), so the loop itself carries no tile-count tests.
+      auto issue = [&](auto two) {
+        constexpr bool kTwo = decltype(two)::value;
+        bool ok = mbar_wait(&q_full[0], 0, abort_flag) &&
+                  (!kTwo || mbar_wait(&q_full[1], 0, abort_flag)) && ring_wait(0);
+        if (ok) {
+          tc_fence_after();
+          qk(0, 0);
+          tc_commit(&s_full[0]);
+          if (kTwo) {
+            qk(1, 0);
+            tc_commit(&s_full[1]);
+          }
+          tc_commit(&kv_empty[0]);
         }
-        tc_commit(&kv_empty[0]);
-      }
-      if constexpr (C::DECOUPLED) {
-        // Per block j: S0(j+1) and S1(j+1) as soon as each softmax has S_t(j) in registers,
-        // then P0(j) V_j and P1(j) V_j as each P arrives; pv_done[t] tells the softmax when
-        // O_t and P_t are free again.
+        if constexpr (C::DECOUPLED) {
+          // Per block j: S0(j+1) and S1(j+1) as soon as each softmax has S_t(j) in registers,
+          // then P0(j) V_j and P1(j) V_j as each P arrives; pv_done[t] tells the softmax when
+          // O_t and P_t are free again.
+          for (int j = 0; j < n && ok; ++j) {
+            const int itV = 2 * j + 1, itK = 2 * j + 2;
+            if (j + 1 < n) {
+              ok = ring_wait(itK) && mbar_wait(&s_free[0], (uint32_t)j & 1u, abort_flag);
+              if (!ok) break;
+              tc_fence_after();
+              qk(0, itK);
+              tc_commit(&s_full[0]);
+              if (kTwo) {
+                if (!(ok = mbar_wait(&s_free[1], (uint32_t)j & 1u, abort_flag))) break;
+                tc_fence_after();
+                qk(1, itK);
+                tc_commit(&s_full[1]);
+              }
+              tc_commit(&kv_empty[itK % C::NSLOT]);
+            }
+            ok = ring_wait(itV) && pv(0, itV, j > 0, j);
+            if (!ok) break;
+            tc_commit(&pv_done[0]);
+            if (kTwo) {
+              if (!(ok = pv(1, itV, j > 0, j))) break;
+              tc_commit(&pv_done[1]);
+            }
+            tc_commit(&kv_empty[itV % C::NSLOT]);
+          }
+        } else {
         for (int j = 0; j < n && ok; ++j) {
           const int itV = 2 * j + 1, itK = 2 * j + 2;
-          if (j + 1 < n) {
-            ok = ring_wait(itK) && mbar_wait(&s_free[0], (uint32_t)j & 1u, abort_flag);
-            if (!ok) break;
+          const bool more = j + 1 < n;
+          ok = ring_wait(itV) && pv(0, itV, j > 0, j);
+          if (!ok) break;
+          if (!more) tc_commit(&o_full[0]);
+          if (more) {
+            if (!(ok = ring_wait(itK))) break;
             tc_fence_after();
             qk(0, itK);
             tc_commit(&s_full[0]);
-            if constexpr (TILES == 2) {
-              if (!(ok = mbar_wait(&s_free[1], (uint32_t)j & 1u, abort_flag))) break;
-              tc_fence_after();
+          }
+          if (kTwo) {
+            if (!(ok = pv(1, itV, j > 0, j))) break;
+          }
+          tc_commit(&kv_empty[itV % C::NSLOT]);
+          if (kTwo && !more) tc_commit(&o_full[1]);
+          if (more) {
+            if (kTwo) {
               qk(1, itK);
               tc_commit(&s_full[1]);
             }
             tc_commit(&kv_empty[itK % C::NSLOT]);
           }
-          ok = ring_wait(itV) && pv(0, itV, j > 0, j);
-          if (!ok) break;
-          tc_commit(&pv_done[0]);
-          if constexpr (TILES == 2) {
-            if (!(ok = pv(1, itV, j > 0, j))) break;
-            tc_commit(&pv_done[1]);
-          }
-          tc_commit(&kv_empty[itV % C::NSLOT]);
         }
+        }
+      };
+      if constexpr (TILES == 2) {
+        if (nt == 2) issue(BoolC<true>{}); else issue(BoolC<false>{});
       } else {
-      for (int j = 0; j < n && ok; ++j) {
-        const int itV = 2 * j + 1, itK = 2 * j + 2;
-        const bool more = j + 1 < n;
-        ok = ring_wait(itV) && pv(0, itV, j > 0, j);
-        if (!ok) break;
-        if (!more) tc_commit(&o_full[0]);
-        if (more) {
-          if (!(ok = ring_wait(itK))) break;
-          tc_fence_after();
-          qk(0, itK);
-          tc_commit(&s_full[0]);
-        }
-        if constexpr (TILES == 2) {
-          if (!(ok = pv(1, itV, j > 0, j))) break;
-        }
-        tc_commit(&kv_empty[itV % C::NSLOT]);
-        if (TILES == 2 && !more) tc_commit(&o_full[1]);
-        if (more) {
-          if constexpr (TILES == 2) {
-            qk(1, itK);
-            tc_commit(&s_full[1]);
-          }
-          tc_commit(&kv_empty[itK % C::NSLOT]);
-        }
-      }
+        issue(BoolC<false>{});
       }
       // Drain: every MMA issued above has completed before TMEM is released.
       tc_commit(mma_done);
@@ -429,14 +463,17 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
     const int col0 = cg * NC;       // first score column of this thread
     const int wq = warp & 3;        // TMEM lane quarter
     const int rt = wq * 32 + lane;  // row within tile
-    const int64_t row = (int64_t)r0 + t * BM + rt;  // row within the sequence
+    const int trow = r0 + t * BM + rt;  // tile row within the (batch, head unit)
+    const int64_t row = trow >> ps;     // query position within the sequence
+    const int h = ps ? (hk << ps) + (trow & pmask) : hu;  // query head of this row
+    const int nj = (TILES == 1 || t < nt) ? n : 0;  // key blocks this tile runs (0: empty tile)
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
     const uint32_t tS = tmem + lane_base + t * 128;
     const uint32_t tO = tmem + lane_base + C::TMEM_O + t * DP;
     const KeyRange kr = key_range(a, sv, row);
     // tile-uniform interval extremes for the "block needs no mask" test
-    const int tile_lo_max = key_range(a, sv, (int64_t)r0 + t * BM + BM - 1).lo;
-    const int tile_hi_min = key_range(a, sv, (int64_t)r0 + t * BM).hi;
+    const int tile_lo_max = key_range(a, sv, (r0 + t * BM + BM - 1) >> ps).lo;
+    const int tile_hi_min = key_range(a, sv, (r0 + t * BM) >> ps).hi;
     constexpr float kLog2e = 1.4426950408889634f;
     // x (the values kept in registers) times c is the logit in log2 units
     const float c = kGeneral ? 1.f : a.scale * kLog2e;
@@ -454,7 +491,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
     float m_used = -INFINITY;  // in x units
     float l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
+    for (int j = 0; j < nj; ++j) {
       ok = __all_sync(kFull, mbar_wait(&s_full[t], (uint32_t)j & 1u, abort_flag));
       if (!ok) break;
       tc_fence_after();
@@ -479,8 +516,11 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
       float lb_slope = 0.f, lb_base = 0.f;
       if constexpr (kBias == 1 && MFA_ALIBI_LINEAR) {
         const float kp0 = (float)(c0 + a.k_pos_offset);  // key position of x[0]
-        const float wmin = centre - (float)lane;         // rows of a warp are consecutive
-        const bool left = kp0 + (float)(NC - 1) <= wmin, right = kp0 >= wmin + 31.f;
+        // smallest and largest centre among the warp's rows (positions ascend with the lane)
+        const int wr0 = r0 + t * BM + wq * 32;
+        const float wmin = (float)((int64_t)(wr0 >> ps) + sv.off);
+        const float wmax = (float)((int64_t)((wr0 + 31) >> ps) + sv.off);
+        const bool left = kp0 + (float)(NC - 1) <= wmin, right = kp0 >= wmax;
         linear_bias = left || right;
         lb_slope = left ? slope_l2 : -slope_l2;  // bias = -slope |c - k| = lb_slope (k - c)
         lb_base = lb_slope * (kp0 - centre);
@@ -650,16 +690,16 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[kPParts * t + kPParts - 1]);
     }
-    if (ok && n > 0) {
+    if (ok && nj > 0) {
       ok = __all_sync(kFull, C::DECOUPLED
-                                 ? mbar_wait(&pv_done[t], (uint32_t)(n - 1) & 1u, abort_flag)
+                                 ? mbar_wait(&pv_done[t], (uint32_t)(nj - 1) & 1u, abort_flag)
                                  : mbar_wait(&o_full[t], 0, abort_flag));
     }
     if constexpr (CG == 2) {
       // row sum = both halves (both threads of a row agree on ok: same barrier waits)
-      *xslot(n & 1, cg) = l;
+      *xslot(nj & 1, cg) = l;
       named_barrier(1 + t, 256);
-      l += *xslot(n & 1, cg ^ 1);
+      l += *xslot(nj & 1, cg ^ 1);
     }
     if (ok) {
       tc_fence_after();
@@ -675,7 +715,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
 #pragma unroll 1
       for (int cc = cg * (DP / CG); cc < (cg + 1) * (DP / CG); cc += 32) {
         float vals[32];
-        if (n > 0) {
+        if (nj > 0) {
           uint32_t o[32];
           tmem_ld32(tO + cc, o);
           tmem_ld_wait32(o);

@@ -165,16 +165,66 @@ struct SplitPlan {
   int split_keys = 0;
   size_t bytes = 0;
 };
+// Bias mode of the tcgen05 kernel: 2 softcap, 1 ALiBi or a non-positive scale, 0 plain.
+int sm100_gen(const mfa_fwd_params* p) {
+  return p->softcap > 0.f ? 2 : (!(p->scale > 0.f) || p->alibi != nullptr) ? 1 : 0;
+}
+int sm100_tiles_rt(bool wide, int gen);
+
+// Query heads packed per KV head (log2; 0 = none). Decode-like launches (fewer than 128 query
+// rows per sequence) of a GQA/MQA model put the query heads of one KV group into the rows of one
+// tile, so each K/V block is loaded once for the whole group instead of once per query head.
+// The group must be a power of two up to 16: the packed Q box is (64, group, 128 / group).
+int pack_shift_for(const mfa_fwd_params* p) {
+#if MFA_PACK_GQA
+  const int g = p->Hq / p->Hkv;
+  const int max_lq = p->cu_q != nullptr ? p->max_lq : p->Lq;
+  if (g < 2 || g > 16 || (g & (g - 1)) != 0 || max_lq >= 128) return 0;
+  int s = 0;
+  while ((1 << s) < g) ++s;
+  return s;
+#else
+  (void)p;
+  return 0;
+#endif
+}
+
+// Decode-like launches (query heads packed, or at most 128 query rows per sequence) run the
+// kPack instantiation in one-tile CTAs, two per SM: a second tile would mostly stay empty, and
+// two CTAs per SM overlap the load -> QK -> softmax -> PV chain of one key block with another's.
+bool sm100_short(const mfa_fwd_params* p) {
+  const int max_lq = p->cu_q != nullptr ? p->max_lq : p->Lq;
+  return pack_shift_for(p) > 0 || max_lq <= 128;
+}
+// Tiles per CTA of the tcgen05 kernel for these params.
+int sm100_tiles_for(const mfa_fwd_params* p) {
+  return sm100_short(p) ? 1 : sm100_tiles_rt(p->D > 64, sm100_gen(p));
+}
+
+#ifndef MFA_MAX_SPLITS
+#define MFA_MAX_SPLITS 128
+#endif
+#ifndef MFA_SPLIT_MIN_BLOCKS
+#define MFA_SPLIT_MIN_BLOCKS 8  // key blocks per split at least
+#endif
+
+// Splits fill one wave of resident CTAs (7/8 of the slots: a split CTA that lands in a second
+// wave doubles the launch's span) with at least 8 key blocks each (below that the per-CTA setup
+// and the merge outweigh the gain). Measured on B200 over decode shapes from 1 to 128 query
+// rows and 2K to 128K keys, this picks the fastest split count or one within a few percent.
 SplitPlan plan_splits(const mfa_fwd_params* p, int sms) {
   SplitPlan sp;
   if (p->cu_q != nullptr || p->B == 0 || p->Lq == 0 || p->Lk == 0) return sp;
-  const int64_t row_blocks = (p->Lq + 255) / 256;
-  const int64_t ctas = row_blocks * p->Hq * p->B;
+  const int ps = pack_shift_for(p);
+  const int tiles = sm100_tiles_for(p);
+  const int64_t rows_per_cta = (int64_t)tiles * 128;
+  const int64_t slots = (int64_t)sms * (tiles == 1 ? 2 : 1);  // resident CTAs
+  const int64_t row_blocks = (((int64_t)p->Lq << ps) + rows_per_cta - 1) / rows_per_cta;
+  const int64_t ctas = row_blocks * (p->Hq >> ps) * p->B;
   const int64_t key_blocks = (p->Lk + 127) / 128;
-  if (ctas >= sms || key_blocks < 4) return sp;
-  int64_t s = (2 * (int64_t)sms + ctas - 1) / ctas;
-  s = s < key_blocks / 2 ? s : key_blocks / 2;
-  s = s < 64 ? s : 64;
+  int64_t s = (slots - slots / 8) / ctas;
+  s = s < key_blocks / MFA_SPLIT_MIN_BLOCKS ? s : key_blocks / MFA_SPLIT_MIN_BLOCKS;
+  s = s < MFA_MAX_SPLITS ? s : MFA_MAX_SPLITS;
   if (s < 2) return sp;
   const int64_t blocks_per = (key_blocks + s - 1) / s;
   sp.split_keys = (int)(blocks_per * 128);
@@ -217,7 +267,7 @@ int pick_kernel(const mfa_fwd_params* p, int dev) {
 
 // 4-D tensor map over (D, H, S, B) with a (64, 1, 128, 1) box and 128-byte swizzle.
 int make_map(CUtensorMap* m, const void* base, int dtype, int D, int H, int64_t S, int B,
-             const int64_t* stride /* batch, seq, head (elements) */) {
+             const int64_t* stride /* batch, seq, head (elements) */, int box_h = 1) {
   auto fn = encode_fn();
   if (fn == nullptr) return MFA_ERR_CUDA;
   const int64_t es = 2;
@@ -229,7 +279,7 @@ int make_map(CUtensorMap* m, const void* base, int dtype, int D, int H, int64_t 
   if (S <= 1) ss = 16;
   if (B <= 1) sbt = 16;
   cuuint64_t strides[3] = {(cuuint64_t)sh, (cuuint64_t)ss, (cuuint64_t)sbt};
-  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_h, (cuuint32_t)(128 / box_h), 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(m, dtype == MFA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                   4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -248,11 +298,12 @@ int sm100_tiles_rt(bool wide, int gen) {
   return gen == 2 ? sm100_tiles<64, 2>() : gen == 1 ? sm100_tiles<64, 1>() : sm100_tiles<64, 0>();
 }
 
-template <int DP, bool BF16, int GEN>
+// SHORT: the one-tile, one-column-group kPack instantiation (sm100_short).
+template <int DP, bool BF16, int GEN, bool SHORT>
 int launch_sm100(const Sm100Args& args, int dev, int64_t grid, cudaStream_t st) {
-  auto k = fa_fwd_sm100<DP, BF16, GEN>;
-  constexpr int CG = DefaultCG<GEN>::value;
-  constexpr int TILES = sm100_tiles<DP, GEN>();
+  constexpr int CG = SHORT ? 1 : DefaultCG<GEN>::value;
+  constexpr int TILES = SHORT ? 1 : sm100_tiles<DP, GEN>();
+  auto k = fa_fwd_sm100<DP, BF16, GEN, CG, TILES, SHORT>;
   using R = sm100::Roles<CG, TILES>;
   const int smem = (int)sm100::Cfg<DP, TILES>::SMEM;
   // The kernel re-splits its registers with setmaxnreg assuming exactly kLaunchRegs per thread
@@ -297,18 +348,25 @@ int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
   if ((rc = make_map(&args.tq, p->q, p->dtype, p->D, p->Hq, Sq, Bm, p->q_stride)) != MFA_OK) return rc;
   if ((rc = make_map(&args.tk, p->k, p->dtype, p->D, p->Hkv, Sk, Bm, p->k_stride)) != MFA_OK) return rc;
   if ((rc = make_map(&args.tv, p->v, p->dtype, p->D, p->Hkv, Sk, Bm, p->v_stride)) != MFA_OK) return rc;
-  const int gen = a.softcap > 0.f ? 2 : (!(a.scale > 0.f) || a.alibi != nullptr) ? 1 : 0;
+  const int gen = sm100_gen(p);
   const bool wide = p->D > 64;
-  const int rows_per_cta = sm100_tiles_rt(wide, gen) * sm100::BM;
-  a.num_row_blocks = (a.max_lq + rows_per_cta - 1) / rows_per_cta;
+  const bool short_rows = sm100_short(p);
+  const int rows_per_cta = (short_rows ? 1 : sm100_tiles_rt(wide, gen)) * sm100::BM;
+  a.pack_shift = pack_shift_for(p);
+  const int heads = p->Hq >> a.pack_shift;  // per batch: query heads, or KV heads when packed
+  if (a.pack_shift > 0 &&
+      (rc = make_map(&args.tqp, p->q, p->dtype, p->D, p->Hq, Sq, Bm, p->q_stride,
+                     1 << a.pack_shift)) != MFA_OK)
+    return rc;
+  a.num_row_blocks = (int)((((int64_t)a.max_lq << a.pack_shift) + rows_per_cta - 1) / rows_per_cta);
   {
     // K/V bytes of one KV head of one sequence; groups of whole KV groups whose K/V stays
     // within ~64 MB of L2 (all of them when everything fits)
     const int64_t kv_unit = (int64_t)(varlen ? p->max_lk : p->Lk) * p->D * 2 * 2;
     int64_t units = kv_unit > 0 ? (64ll << 20) / kv_unit : (1ll << 30);
     if (units < 1) units = 1;
-    const int64_t all = (int64_t)p->Hq * a.B;
-    const int64_t ghb = units * (p->Hq / p->Hkv);
+    const int64_t all = (int64_t)heads * a.B;
+    const int64_t ghb = units * (p->Hq / p->Hkv >> a.pack_shift);
     a.group_hb = (int)(ghb < all ? ghb : all);
   }
   FwdArgs fin = a;  // the caller's output, for the split merge
@@ -336,13 +394,14 @@ int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
     a.lse_split_stride = rows;
   }
   args.a = a;
-  const int64_t grid = (int64_t)a.num_row_blocks * a.Hq * a.B * a.num_splits;
+  const int64_t grid = (int64_t)a.num_row_blocks * heads * a.B * a.num_splits;
   if (grid == 0) return MFA_OK;
   if (grid >= (1ll << 31)) return MFA_ERR_UNSUPPORTED;
   const bool bf = p->dtype == MFA_BF16;
 #define MFA_SM100(DP, BF, G)                                                     \
   do {                                                                           \
-    const int rc_ = launch_sm100<DP, BF, G>(args, dev, grid, st);                \
+    const int rc_ = short_rows ? launch_sm100<DP, BF, G, true>(args, dev, grid, st)   \
+                               : launch_sm100<DP, BF, G, false>(args, dev, grid, st); \
     if (rc_ != MFA_OK || split.splits < 2) return rc_;                           \
     return launch_combine(fin, ws_o, ws_lse, p->o, p->lse, st);                  \
   } while (0)
@@ -455,6 +514,15 @@ int mfa_fwd_num_splits(const mfa_fwd_params* p) {
   if (mfa::pick_kernel(p, dev) != MFA_KERNEL_TCGEN05 || p->workspace == nullptr) return 1;
   const mfa::SplitPlan sp = mfa::plan_splits(p, mfa::dev_info(dev).sms);
   return (sp.splits > 1 && p->workspace_bytes >= sp.bytes) ? sp.splits : 1;
+}
+
+int mfa_fwd_packed_heads(const mfa_fwd_params* p) {
+  int rc = mfa::validate(p);
+  if (rc != MFA_OK) return -rc;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -MFA_ERR_NO_DEVICE;
+  if (mfa::pick_kernel(p, dev) != MFA_KERNEL_TCGEN05) return 1;
+  return 1 << mfa::pack_shift_for(p);
 }
 
 int mfa_select_kernel(const mfa_fwd_params* p) {
