@@ -196,11 +196,16 @@ __global__ void lse_combine_kernel(const __grid_constant__ PartPtrs pp, int n, i
 
 // Merge of the key splits of one launch (dense layout): partial outputs ws_o fp32
 // [split][B][Lq][Hq][D] normalised by their own sums, row log-sum-exp ws_lse [split][B][Hq][Lq].
-// One block of kCombineThreads per (batch, head, row): the split weights exp(lse_s - max) are
-// computed in parallel into shared memory (a.num_splits floats of dynamic shared memory), then
-// each thread sums its output columns over the splits with independent loads; the final row is
-// written in the caller's dtype and strides.
-constexpr int kCombineThreads = 128;
+// One block of kCombineThreads per (batch, head, row). The split weights exp(lse_s - max) are
+// computed in parallel into shared memory (a.num_splits floats of dynamic shared memory); then
+// warp w sums the splits w, w + 8, ... of the row, each lane four columns with 16-byte loads, so
+// a thread's loads are independent of one another; the eight warp sums meet in shared memory
+// and the final row is written in the caller's dtype and strides. D is a multiple of 8 (the
+// tcgen05 path's requirement) and the workspace is 256-byte aligned, so the loads are aligned.
+// The kernel is launched as a programmatic dependent of the forward: griddepcontrol.wait holds
+// it until the forward grid has finished and its writes are visible.
+constexpr int kCombineThreads = 256;
+constexpr int kCombineWarps = kCombineThreads / 32;
 __device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -212,7 +217,7 @@ __device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) 
   if (lane == 0) red[warp] = v;
   __syncthreads();
   v = red[0];
-  for (int w = 1; w < kCombineThreads / 32; ++w) v = is_max ? fmaxf(v, red[w]) : v + red[w];
+  for (int w = 1; w < kCombineWarps; ++w) v = is_max ? fmaxf(v, red[w]) : v + red[w];
   return v;
 }
 
@@ -221,7 +226,9 @@ __global__ void __launch_bounds__(kCombineThreads)
     split_combine_kernel(const FwdArgs a, const float* __restrict__ ws_o,
                          const float* __restrict__ ws_lse, TO* o, float* lse_out) {
   extern __shared__ float sw[];  // [num_splits]
-  __shared__ float red[kCombineThreads / 32];
+  __shared__ float red[kCombineWarps];
+  __shared__ float4 part[kCombineWarps][32];  // per-warp column sums (D <= 128)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int64_t w = blockIdx.x;
   const int row = (int)(w % a.Lq);
   const int bh = (int)(w / a.Lq);
@@ -243,16 +250,36 @@ __global__ void __launch_bounds__(kCombineThreads)
   }
   tot = block_reduce(tot, false, red);  // its barriers also publish sw
   const float inv = tot > 0.f ? 1.f / tot : 0.f;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool has_cols = 4 * lane < a.D;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (has_cols) {
+    const float4* src = reinterpret_cast<const float4*>(ws_o + oi) + lane;
+    const int64_t step = ostride / 4;  // float4 per split
+#pragma unroll 4
+    for (int s = warp; s < S; s += kCombineWarps) {
+      const float4 x = src[s * step];
+      const float ws = sw[s];
+      acc.x = fmaf(ws, x.x, acc.x);
+      acc.y = fmaf(ws, x.y, acc.y);
+      acc.z = fmaf(ws, x.z, acc.z);
+      acc.w = fmaf(ws, x.w, acc.w);
+    }
+  }
+  part[warp][lane] = acc;
+  __syncthreads();
+  // thread t < D writes column t: the sum over the warps of lane t/4's component t%4
   TO* orow = o + (int64_t)b * a.o_sb + (int64_t)row * a.o_ss + (int64_t)h * a.o_sh;
   for (int d = threadIdx.x; d < a.D; d += kCombineThreads) {
-    float acc = 0.f;
-#pragma unroll 8
-    for (int s = 0; s < S; ++s) acc = fmaf(sw[s], ws_o[s * ostride + oi + d], acc);
-    acc *= inv;
+    const float* pc = reinterpret_cast<const float*>(&part[0][0]) + d;  // column d of warp 0
+    float v = 0.f;
+#pragma unroll
+    for (int q = 0; q < kCombineWarps; ++q) v += pc[q * 128];
+    v *= inv;
     if constexpr (sizeof(TO) == 4) {
-      orow[d] = acc;
+      orow[d] = v;
     } else {
-      orow[d] = TO(acc);
+      orow[d] = TO(v);
     }
   }
   if (threadIdx.x == 0 && lse_out != nullptr)

@@ -242,6 +242,9 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
   const SeqView sv = seq_view(a, b);
   const int rows = sv.lq << ps;  // tile rows of this (batch, head unit)
   const int r0 = rb * TILES * BM;
+  // a split launch is followed by its merge, launched as a programmatic dependent: let it be
+  // scheduled now (it waits for this grid's completion before reading anything)
+  if (a.num_splits > 1) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (r0 >= rows) return;  // whole CTA leaves before touching barriers or TMEM
   // tiles holding at least one row (a last row block may leave the second tile empty)
   const int nt = (TILES == 2 && r0 + BM < rows) ? 2 : 1;

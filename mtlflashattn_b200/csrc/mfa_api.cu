@@ -325,15 +325,27 @@ int launch_combine(const FwdArgs& fin, const float* ws_o, const float* ws_lse, v
   const int64_t rows = (int64_t)fin.B * fin.Hq * fin.Lq;
   if (rows == 0) return MFA_OK;
   if (rows >= (1ll << 31)) return MFA_ERR_UNSUPPORTED;
-  const unsigned blocks = (unsigned)rows;
-  const int smem = fin.num_splits * (int)sizeof(float);
+  // a programmatic dependent launch: the merge grid is set up while the forward drains and
+  // waits (griddepcontrol.wait) for its completion before reading the partials
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)rows);
+  cfg.blockDim = dim3(kCombineThreads);
+  cfg.dynamicSmemBytes = (size_t)fin.num_splits * sizeof(float);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
   if (fin.o_dtype == MFA_FP32)
-    split_combine_kernel<float><<<blocks, kCombineThreads, smem, st>>>(fin, ws_o, ws_lse, (float*)o, lse);
+    e = cudaLaunchKernelEx(&cfg, split_combine_kernel<float>, fin, ws_o, ws_lse, (float*)o, lse);
   else if (fin.o_dtype == MFA_BF16)
-    split_combine_kernel<__nv_bfloat16><<<blocks, kCombineThreads, smem, st>>>(fin, ws_o, ws_lse, (__nv_bfloat16*)o, lse);
+    e = cudaLaunchKernelEx(&cfg, split_combine_kernel<__nv_bfloat16>, fin, ws_o, ws_lse,
+                           (__nv_bfloat16*)o, lse);
   else
-    split_combine_kernel<__half><<<blocks, kCombineThreads, smem, st>>>(fin, ws_o, ws_lse, (__half*)o, lse);
-  return MFA_OK;
+    e = cudaLaunchKernelEx(&cfg, split_combine_kernel<__half>, fin, ws_o, ws_lse, (__half*)o, lse);
+  return e == cudaSuccess ? MFA_OK : MFA_ERR_CUDA;
 }
 
 int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
