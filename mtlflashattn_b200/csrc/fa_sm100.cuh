@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
   int khi = key_range(a, sv, r_last >> ps).hi;
   if (a.num_splits > 1) {
     klo = max(klo, split * a.split_keys);
-    khi = min(khi, (split + 1) * a.split_keys);
+    if (split + 1 < a.num_splits) khi = min(khi, (split + 1) * a.split_keys);
   }
   const int jb = klo / BN;
   const int n = khi > klo ? (khi + BN - 1) / BN - jb : 0;

@@ -212,25 +212,32 @@ int sm100_tiles_for(const mfa_fwd_params* p) {
 // wave doubles the launch's span) with at least 8 key blocks each (below that the per-CTA setup
 // and the merge outweigh the gain). Measured on B200 over decode shapes from 1 to 128 query
 // rows and 2K to 128K keys, this picks the fastest split count or one within a few percent.
+// Varlen launches split by the longest sequence's keys (max_lk); every split CTA of a shorter
+// sequence whose keys end before its range writes an empty partial (weight 0 in the merge), and
+// the last split takes all keys past its start, so an understated max_lk loses nothing.
 SplitPlan plan_splits(const mfa_fwd_params* p, int sms) {
   SplitPlan sp;
-  if (p->cu_q != nullptr || p->B == 0 || p->Lq == 0 || p->Lk == 0) return sp;
+  const bool varlen = p->cu_q != nullptr;
+  const int64_t lq = varlen ? p->max_lq : p->Lq;
+  const int64_t lk = varlen ? p->max_lk : p->Lk;
+  if (p->B == 0 || lq <= 0 || lk <= 0) return sp;
   const int ps = pack_shift_for(p);
   const int tiles = sm100_tiles_for(p);
   const int64_t rows_per_cta = (int64_t)tiles * 128;
   const int64_t slots = (int64_t)sms * (tiles == 1 ? 2 : 1);  // resident CTAs
-  const int64_t row_blocks = (((int64_t)p->Lq << ps) + rows_per_cta - 1) / rows_per_cta;
+  const int64_t row_blocks = ((lq << ps) + rows_per_cta - 1) / rows_per_cta;
   const int64_t ctas = row_blocks * (p->Hq >> ps) * p->B;
-  const int64_t key_blocks = (p->Lk + 127) / 128;
+  const int64_t key_blocks = (lk + 127) / 128;
   int64_t s = (slots - slots / 8) / ctas;
   s = s < key_blocks / MFA_SPLIT_MIN_BLOCKS ? s : key_blocks / MFA_SPLIT_MIN_BLOCKS;
   s = s < MFA_MAX_SPLITS ? s : MFA_MAX_SPLITS;
   if (s < 2) return sp;
   const int64_t blocks_per = (key_blocks + s - 1) / s;
   sp.split_keys = (int)(blocks_per * 128);
-  sp.splits = (int)((p->Lk + sp.split_keys - 1) / sp.split_keys);
+  sp.splits = (int)((lk + sp.split_keys - 1) / sp.split_keys);
   if (sp.splits < 2) return SplitPlan{};
-  const size_t rows = (size_t)p->B * p->Hq * p->Lq;
+  // partial rows: [B][Lq][Hq] dense, [total_q][Hq] varlen (Lq carries total_q)
+  const size_t rows = (size_t)(varlen ? 1 : p->B) * p->Hq * p->Lq;
   sp.bytes = (size_t)sp.splits * rows * ((size_t)p->D + 1) * sizeof(float) + 256;
   return sp;
 }
@@ -383,13 +390,14 @@ int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
   }
   FwdArgs fin = a;  // the caller's output, for the split merge
   fin.num_splits = split.splits;
+  if (varlen) fin.B = 1;  // the merge walks the packed rows [total_q][Hq] as one batch
   float* ws_o = nullptr;
   float* ws_lse = nullptr;
   if (split.splits > 1) {
     // partials: fp32 [split][B][Lq][Hq][D] and row lse [split][B][Hq][Lq] in the workspace
     uintptr_t base = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~(uintptr_t)255;
     ws_o = reinterpret_cast<float*>(base);
-    const int64_t rows = (int64_t)p->B * p->Hq * p->Lq;
+    const int64_t rows = (int64_t)(varlen ? 1 : p->B) * p->Hq * p->Lq;
     ws_lse = ws_o + (int64_t)split.splits * rows * p->D;
     a.o = ws_o;
     a.o_dtype = MFA_FP32;

@@ -72,3 +72,71 @@ def test_split_writes_row_lse():
 def test_no_split_when_grid_is_full():
     q, k, v = (torch.empty(1, 8192, 16, 128, device=DEV, dtype=torch.bfloat16) for _ in range(3))
     assert plan(q, k, v) == (0, 1)
+
+
+def varlen_plan(q, k, v, cu_q, cu_k, max_lq, max_lk):
+    """(workspace bytes, splits) the library chooses for a varlen call."""
+    o = torch.empty_like(q)
+    p = _kernel._params(q, k, v, o, B=cu_q.shape[0] - 1, Hq=q.shape[1], Hkv=k.shape[1],
+                        Lq=q.shape[0], Lk=k.shape[0], D=q.shape[2],
+                        q_st=(0, q.stride(0), q.stride(1)), k_st=(0, k.stride(0), k.stride(1)),
+                        v_st=(0, v.stride(0), v.stride(1)), o_st=(0, o.stride(0), o.stride(1)),
+                        scale=1.0, causal=True, bias=_kernel._BiasParams(0.0, -1, -1, None),
+                        kernel=_lib.KERNEL_AUTO, cu_q=cu_q, cu_k=cu_k, max_lq=max_lq,
+                        max_lk=max_lk)
+    need = _lib.workspace_size(p)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=DEV)
+    p.workspace, p.workspace_bytes = ws.data_ptr(), need
+    return need, _lib.num_splits(p)
+
+
+VARLEN_CASES = [
+    # lens_q, lens_k, Hq, Hkv, D, dtype, kwargs
+    ([1] * 8, [8192, 300, 5000, 1, 8192, 2048, 7000, 4096], 32, 8, 128, torch.bfloat16,
+     dict(causal=True)),
+    ([1, 2, 0, 1], [30000, 0, 100, 12000], 16, 2, 128, torch.float16, dict(causal=True)),
+    ([4, 1, 3], [20000, 20000, 9000], 8, 8, 64, torch.bfloat16,
+     dict(causal=True, window_size=(4000, 0))),
+    ([1, 1], [16000, 9000], 8, 2, 128, torch.bfloat16, dict(softcap=25.0)),
+    ([2, 1, 1], [10000, 600, 15000], 8, 2, 128, torch.bfloat16, dict(alibi_slopes="per-seq")),
+]
+
+
+@pytest.mark.parametrize("case", VARLEN_CASES, ids=[f"v{i}" for i in range(len(VARLEN_CASES))])
+def test_varlen_split_matches_oracle(case):
+    lq, lk, Hq, Hkv, D, dtype, kw = case
+    q, k, v, cu_q, cu_k = ref.make_varlen(lq, lk, Hq, Hkv, D, dtype, seed=sum(lk) % 1000)
+    if kw.get("alibi_slopes") == "per-seq":
+        kw = dict(kw, alibi_slopes=torch.rand(len(lq), Hq, generator=torch.Generator().manual_seed(1)) * 0.05)
+    qd, kd, vd, cqd, ckd = (t.to(DEV) for t in (q, k, v, cu_q, cu_k))
+    need, splits = varlen_plan(qd, kd, vd, cqd, ckd, max(lq), max(lk))
+    assert need > 0 and splits > 1, (need, splits)
+    kwd = {a: (b.to(DEV) if torch.is_tensor(b) else b) for a, b in kw.items()}
+    out = mfa.flash_attn_varlen_func(qd, kd, vd, cqd, ckd, max(lq), max(lk), **kwd)
+    want = ref.flash_attn_varlen_func(q, k, v, cu_q, cu_k, **kw)
+    torch.testing.assert_close(out.float().cpu(), want, **TOL[dtype])
+
+
+def test_varlen_split_row_lse_and_understated_max_lk():
+    """The row log-sum-exp of a split varlen launch, and a max_lk below the true longest key
+    length (the last split takes every remaining key, so nothing is lost)."""
+    lq, lk = [1, 3, 2], [9000, 20000, 4000]
+    Hq, Hkv, D = 16, 4, 128
+    q, k, v, cu_q, cu_k = ref.make_varlen(lq, lk, Hq, Hkv, D, torch.bfloat16, seed=21)
+    qd, kd, vd, cqd, ckd = (t.to(DEV) for t in (q, k, v, cu_q, cu_k))
+    scale = 1 / math.sqrt(D)
+    want = ref.flash_attn_varlen_func(q, k, v, cu_q, cu_k, causal=True)
+    for max_lk in (max(lk), 12000):
+        assert varlen_plan(qd, kd, vd, cqd, ckd, max(lq), max_lk)[1] > 1
+        o = torch.empty_like(qd)
+        lse = torch.empty(Hq, q.shape[0], device=DEV, dtype=torch.float32)
+        _kernel.forward_varlen(qd, kd, vd, o, cqd, ckd, max(lq), max_lk, scale, True,
+                               _kernel._BiasParams(0.0, -1, -1, None), lse=lse)
+        torch.testing.assert_close(o.float().cpu(), want, **TOL[torch.bfloat16])
+        for i in range(len(lq)):
+            qs = slice(int(cu_q[i]), int(cu_q[i + 1]))
+            ks = slice(int(cu_k[i]), int(cu_k[i + 1]))
+            _, wl = ref.attention_heads_second(q[qs].permute(1, 0, 2)[None], k[ks].permute(1, 0, 2)[None],
+                                               v[ks].permute(1, 0, 2)[None], scale, True,
+                                               return_lse=True)
+            torch.testing.assert_close(lse[:, qs].cpu(), wl[0], atol=1e-3, rtol=1e-4)
