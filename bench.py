@@ -1,18 +1,29 @@
 """Benchmark: attention forward throughput (causal-adjusted TFLOP/s) on 1..8 B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5|target] [--impl reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 1|2|3|4|5|target] [--impl reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
-One step = one forward of the workload over inputs already resident in HBM (``value``), and,
-separately, the same workload through the public host-memory API (``flash_attn_host``) with
-pinned host inputs copied in and the output copied back inside the timed region (``e2e``).
-The default workload is BASELINE config 2 (B=1, H=16, L=8192, D=64, bf16, causal). With N ranks
-each rank runs its own instance (batch-sharded, no collective: weak scaling), except config 5
-(one 131072-token sequence), whose heads are sharded over the ranks (strong scaling); the
-reported time is the max over ranks.
+The default workload is BASELINE config 5, the one the metric quotes at 1/2/4/8 GPUs: one
+131072-token sequence, B=1 H=16 D=128 bf16 causal, inputs 0.5*N(0,1). One step = one forward of
+the whole problem over inputs already resident in HBM (``value``). With N ranks the heads are
+sharded over the ranks (KV-group-aligned, no communication): strong scaling, ``value`` = the
+whole problem's FLOPs over the max-over-ranks device time. At N > 1 the same line carries a
+``split_kv`` leg: every rank holds the zigzag key chunks g and 2N-1-g of all heads, computes
+partials for every query row, and the partials are merged over NCCL (all-gather of the row
+log-sum-exp, one rescale kernel, reduce-scatter by query rows); its rate and the collectives'
+share of each step are timed with CUDA events. Every run checks sampled row windows of its
+output against a single-GPU forward of the same rows (``parity``).
 
-``--impl reference`` times the reference's own CPU algorithm (the chunked-fp32 torch tier,
-restated in oracle/flash_torch.py) on the host cores, on a bounded sample of the same workload.
+``e2e`` is the same workload through the public host-memory API (``flash_attn_host``): pinned
+host inputs copied in and the output copied back inside the timed region.
+
+At N = 1 the line also carries ``configs``: BASELINE configs 1, 2, 3, 4 and the D=128 target,
+each timed on the device the same way, and ``cpu_baseline``: the reference's CPU algorithm (the
+chunked-fp32 torch tier, restated in oracle/flash_torch.py) on a bounded sample of config 5 and
+on all of config 1.
+
+``--impl reference`` times the reference's own CPU algorithm on the host cores, on a bounded
+sample of the same workload.
 """
 from __future__ import annotations
 
@@ -34,6 +45,7 @@ from mtlflashattn_b200.flops import attention_flops, compulsory_bytes, varlen_fl
 
 METRIC = "attn fwd causal-adjusted TFLOP/s at 1/2/4/8 B200; % of dense TC peak"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+SUB_CONFIGS = ("2", "target", "3", "4", "1")
 
 
 def peaks():
@@ -47,26 +59,25 @@ def peaks():
 
 
 # ------------------------------------------------------------------------------ workloads
+DENSE = {
+    # name: (B, L, H, D, dtype, causal, kwargs, input scale)
+    "1": (1, 1024, 4, 64, torch.float32, False, {}, 1.0),
+    "2": (1, 8192, 16, 64, torch.bfloat16, True, {}, 1.0),
+    "3": (1, 8192, 16, 128, torch.float16, False, dict(softcap=30.0, window_size=(1024, 1024)), 1.0),
+    "target": (1, 8192, 16, 128, torch.bfloat16, True, {}, 1.0),
+    "5": (1, 131072, 16, 128, torch.bfloat16, True, {}, 0.5),
+}
+
+
 def workload(cfg, device, rank=0, world=1):
     """Synthetic inputs with the BASELINE config's shapes and distributions (N(0,1), seeded).
     Returns (call(q, k, v) launching exactly one kernel, host inputs, algorithmic FLOPs,
-    compulsory HBM bytes, description)."""
+    compulsory HBM bytes, description). Config 5 at world > 1 gives this rank its heads."""
     import mtlflashattn_b200 as mfa
 
     g = torch.Generator().manual_seed(1000 + rank)
-    if cfg in ("2", "3", "target", "5"):
-        if cfg == "2":
-            B, L, H, D, dt, causal, kw = 1, 8192, 16, 64, torch.bfloat16, True, {}
-        elif cfg == "3":
-            B, L, H, D, dt, causal, kw = 1, 8192, 16, 128, torch.float16, False, dict(
-                softcap=30.0, window_size=(1024, 1024))
-        elif cfg == "target":
-            B, L, H, D, dt, causal, kw = 1, 8192, 16, 128, torch.bfloat16, True, {}
-        else:
-            B, L, H, D, dt, causal, kw = 1, 131072, 16, 128, torch.bfloat16, True, {}
-        sc = 0.5 if cfg == "5" else 1.0
-        # config 5 on N ranks: one sequence, head-sharded (each rank its KV-group-aligned heads,
-        # no communication): strong scaling of the whole problem
+    if cfg in DENSE:
+        B, L, H, D, dt, causal, kw, sc = DENSE[cfg]
         strong = cfg == "5" and world > 1
         Hr = H
         if strong:
@@ -78,7 +89,7 @@ def workload(cfg, device, rank=0, world=1):
         k = (torch.randn(B, L, Hr, D, generator=g) * sc).to(dt)
         v = (torch.randn(B, L, Hr, D, generator=g) * sc).to(dt)
         flops = attention_flops(B, Hr, L, L, D, causal, kw.get("window_size", (-1, -1)))
-        nbytes = compulsory_bytes(B, Hr, Hr, L, L, D)
+        nbytes = compulsory_bytes(B, Hr, Hr, L, L, D, elem=q.element_size())
 
         def call(q, k, v):
             return mfa.flash_attn_func(q, k, v, causal=causal, **kw)
@@ -88,13 +99,14 @@ def workload(cfg, device, rank=0, world=1):
                                        synchronize=False, **kw)
 
         call.host = host_call
-
-        desc = dict(workload=f"config{cfg}" if cfg != "target" else "target", batch_per_rank=B,
-                    seq_len=L, heads=H, head_dim=D, dtype=str(dt).replace("torch.", ""),
-                    causal=causal, **{k_: list(v_) if isinstance(v_, tuple) else v_
-                                      for k_, v_ in kw.items()})
+        name = "target" if cfg == "target" else f"config{cfg}"
+        desc = dict(workload=name, batch_per_rank=B, seq_len=L, heads=H, head_dim=D,
+                    dtype=str(dt).replace("torch.", ""), causal=causal,
+                    **{k_: list(v_) if isinstance(v_, tuple) else v_ for k_, v_ in kw.items()})
+        if sc != 1.0:
+            desc["input_scale"] = sc
         if strong:
-            desc.update(heads_per_rank=Hr, strong=True,
+            desc.update(heads_per_rank=Hr, strong=True, head_range=[h0, h1],
                         total_flops=attention_flops(B, H, L, L, D, causal, (-1, -1)))
         return call, (q, k, v), flops, nbytes, desc
     if cfg == "4":
@@ -121,7 +133,6 @@ def workload(cfg, device, rank=0, world=1):
                                               synchronize=False)
 
         call.host = host_call
-
         desc = dict(workload="config4", sequences=16, total_tokens=tot, heads_q=32, heads_kv=8,
                     head_dim=128, dtype="bfloat16", causal=True, alibi=True)
         return call, (q, k, v), flops, nbytes, desc
@@ -186,40 +197,66 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------- CPU leg
+
+# ------------------------------------------------------------------------------- CPU leg
 def cpu_sample_run(reps_budget_s=10.0, steps=None, rows=512):
     """Time the reference's CPU algorithm (oracle port of the chunked-fp32 torch tier) on a
-    bounded sample of config 2: one head, ``rows`` query rows centred in the middle of the
-    sequence (their mean causal key count equals the full problem's), all 8192 keys, bf16
-    inputs. Returns (TFLOP/s over the sample's algorithmic FLOPs, seconds per sample,
+    bounded sample of config 5: one head, ``rows`` query rows centred in the middle of the
+    131072-token sequence (their mean causal key count equals the full problem's), bf16 inputs
+    0.5*N(0,1). Returns (TFLOP/s over the sample's algorithmic FLOPs, seconds per sample,
     description)."""
     from oracle import flash_torch as ref
 
-    L, D, r = 8192, 64, rows
+    L, D, r = 131072, 128, rows
     r0 = L // 2 - r // 2
     g = torch.Generator().manual_seed(0)
-    q = torch.randn(1, r, 1, D, generator=g).bfloat16()
-    k = torch.randn(1, L, 1, D, generator=g).bfloat16()
-    v = torch.randn(1, L, 1, D, generator=g).bfloat16()
+    q = (torch.randn(1, r, 1, D, generator=g) * 0.5).bfloat16()
+    k = (torch.randn(1, r0 + r, 1, D, generator=g) * 0.5).bfloat16()
+    v = (torch.randn(1, r0 + r, 1, D, generator=g) * 0.5).bfloat16()
     qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
     flops = 4 * D * sum(r0 + i + 1 for i in range(r))
 
     def one():
-        ref.attention_heads_second(qh, kh, vh, 1 / math.sqrt(D), True, row_offset=r0,
-                                   lq_total=L).to(torch.bfloat16)
+        # rows [r0, r0 + r) of the full problem: bottom-right causal over keys [0, r0 + r)
+        ref.attention_heads_second(qh, kh, vh, 1 / math.sqrt(D), True).to(torch.bfloat16)
 
     one()  # warm-up
     times = []
     t_end = time.perf_counter() + reps_budget_s
     n = 0
-    while (steps is None and time.perf_counter() < t_end) or (steps is not None and n < steps):
+    while (steps is None and (time.perf_counter() < t_end or n == 0)) or (steps is not None and n < steps):
         t0 = time.perf_counter()
         one()
         times.append(time.perf_counter() - t0)
         n += 1
     t = statistics.median(times)
-    desc = (f"config2 sample: 1 of 16 heads, query rows [{r0},{r0 + r}) of 8192 (mean causal "
-            f"key count = full problem's), all 8192 keys; {n} timed repetitions, median")
+    desc = (f"config5 sample: 1 of 16 heads, query rows [{r0},{r0 + r}) of 131072 against their "
+            f"causal key prefix (mean key count = the full problem's, so the rate extrapolates to "
+            f"the full problem; the full problem is 16 heads x 131072 rows); {n} timed "
+            f"repetitions, median")
     return flops / t / 1e12, t, desc
+
+
+def cpu_config1_run(reps_budget_s=5.0):
+    """The reference's stated CPU run, whole and unsampled: BASELINE config 1 (B=1 H=4
+    Lq=Lk=1024 D=64 fp32, q/k/v N(0,1) from seed 0, non-causal, scale 1/8) through the chunked
+    fp32 torch tier (oracle port), timed like the reference's bench loop (bench/bench_attn.py:
+    14-22: warm-up, then the median of timed repetitions)."""
+    from oracle import flash_torch as ref
+
+    q, k, v = ref.make_qkv(1, 1024, 1024, 4, 4, 64, torch.float32, seed=0)
+    flops = attention_flops(1, 4, 1024, 1024, 64, False)
+    for _ in range(3):
+        ref.flash_attn_func(q, k, v, softmax_scale=0.125)
+    times = []
+    t_end = time.perf_counter() + reps_budget_s
+    while time.perf_counter() < t_end or len(times) < 5:
+        t0 = time.perf_counter()
+        ref.flash_attn_func(q, k, v, softmax_scale=0.125)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return dict(value=round(flops / t / 1e12, 6), unit="TFLOP/s", ms=round(t * 1e3, 3),
+                reps=len(times), sample="all of config 1 (B=1 H=4 L=1024 D=64 fp32, non-causal)")
 
 
 def run_reference(args):
@@ -229,18 +266,18 @@ def run_reference(args):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     # size the per-step sample so the whole --steps/--warmup run stays within ~2 minutes
-    _, t512, _ = cpu_sample_run(steps=1, rows=512)
+    _, t256, _ = cpu_sample_run(steps=1, rows=256)
     budget = 120.0 / max(1, args.steps + args.warmup)
-    rows = int(max(16, min(512, 512 * budget / max(t512, 1e-6))) // 16 * 16)
+    rows = int(max(16, min(1024, 256 * budget / max(t256, 1e-6))) // 16 * 16)
     for _ in range(args.warmup):
         cpu_sample_run(steps=1, rows=rows)
     tf, t, desc = cpu_sample_run(steps=args.steps, rows=rows)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(tf, 6), "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(t * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
-        "config": dict(workload="config2", seq_len=8192, heads=16, head_dim=64, causal=True,
+        "ms_per_step": round(t * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded 0.5*N(0,1))",
+        "config": dict(workload="config5", seq_len=131072, heads=16, head_dim=128, causal=True,
                        dtype_inputs="bfloat16", parallelism="host CPU"),
         "cpu_baseline": {"value": round(tf, 6), "unit": "TFLOP/s", "cores": threads,
                          "kind": "port", "sample": desc},
@@ -266,6 +303,113 @@ def timed_steps(fn, steps, flush_buf, stream):
     return [s.elapsed_time(e) for s, e in evs]
 
 
+def window_diff(q, k, v, out, windows, row0=0):
+    """Largest |out - reference| over sampled query-row windows of a bottom-right causal
+    problem with Lq == Lk. Rows [r0, r1) of the full problem equal a forward with Lq = r1 - r0
+    over keys [0, r1), run here as a separate single-GPU forward. ``out`` holds the rows from
+    ``row0`` on (a rank's own rows after a split-KV merge)."""
+    import mtlflashattn_b200 as mfa
+
+    worst = 0.0
+    for r0, r1 in windows:
+        w = mfa.flash_attn_func(q[:, r0:r1], k[:, :r1], v[:, :r1], causal=True)
+        got = out[:, r0 - row0:r1 - row0]
+        worst = max(worst, (w.float() - got.float()).abs().max().item())
+    return worst
+
+
+def sample_windows(lo, hi, width=512, n=5):
+    """n windows of `width` rows spread over [lo, hi), first and last included."""
+    if hi - lo <= width:
+        return [(lo, hi)] if hi > lo else []
+    starts = sorted({lo + (hi - width - lo) * i // (n - 1) for i in range(n)})
+    return [(a, a + width) for a in starts]
+
+
+def measure(cfg, dev, steps, warmup, flush, stream, rank=0, world=1):
+    """Device time of `steps` forwards of workload `cfg` (inputs resident). Returns (per-step
+    ms list, flops, nbytes, desc, call, device inputs, host inputs, last output)."""
+    call, host_in, flops, nbytes, desc = workload(cfg, dev, rank, world)
+    dev_in = [t.to(dev) for t in host_in]
+    last = []
+
+    def step():
+        last[:] = [call(*dev_in)]
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    times = timed_steps(step, steps, flush, stream)
+    return times, flops, nbytes, desc, call, dev_in, host_in, last[0]
+
+
+def split_kv_leg(steps, warmup, dev, rank, world, flush, stream, dist):
+    """Config 5 as split-KV over the ranks: rank g holds the zigzag key chunks g and 2N-1-g of
+    every head (all ranks draw the same seeded q/k/v on the device), computes partials for all
+    131072 query rows and the merge leaves each rank its own rows. Per step, CUDA events on the
+    launching stream time the forwards, the log-sum-exp all-gather, the rescale kernel and the
+    reduce-scatter; every figure is the max over ranks."""
+    from mtlflashattn_b200 import distributed as mfd
+
+    B, L, H, D, dt, causal, _, sc = DENSE["5"]
+    gen = torch.Generator(device=dev).manual_seed(2024)
+    q = (torch.randn(B, L, H, D, device=dev, generator=gen) * sc).to(dt)
+    k = (torch.randn(B, L, H, D, device=dev, generator=gen) * sc).to(dt)
+    v = (torch.randn(B, L, H, D, device=dev, generator=gen) * sc).to(dt)
+    rng = mfd.zigzag_ranges(L, world, rank)
+    kp = [k[:, a:b].contiguous() for a, b in rng]
+    vp = [v[:, a:b].contiguous() for a, b in rng]
+    last = []
+
+    def one(ev=None):
+        last[:] = [mfd.flash_attn_split_kv(q, kp, vp, rng, L, causal=True, events=ev)]
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    dist.barrier()
+    parts = []
+    for _ in range(steps):
+        flush.zero_()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        ev = {}
+        s.record(stream)
+        one(ev)
+        e.record(stream)
+        parts.append((s, e, ev))
+    torch.cuda.synchronize()
+    tot = fwd = gat = resc = rs = 0.0
+    for s, e, ev in parts:
+        tot += s.elapsed_time(e)
+        fwd += s.elapsed_time(ev["forward_done"])
+        gat += ev["lse_gather"][0].elapsed_time(ev["lse_gather"][1])
+        resc += ev["lse_gather"][1].elapsed_time(ev["reduce_scatter"][0])
+        rs += ev["reduce_scatter"][0].elapsed_time(ev["reduce_scatter"][1])
+    t = torch.tensor([tot, fwd, gat, resc, rs], device=dev, dtype=torch.float64) / steps
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    tot, fwd, gat, resc, rs = t.tolist()
+    out, (r0, r1) = last[0]
+    diff = window_diff(q, k, v, out, sample_windows(r0, r1), row0=r0)
+    dd = torch.tensor([diff], device=dev, dtype=torch.float64)
+    dist.all_reduce(dd, op=dist.ReduceOp.MAX)
+    flops = attention_flops(B, H, L, L, D, causal)
+    return {
+        "value": round(flops / (tot * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+        "ms_per_step": round(tot, 4), "steps": steps,
+        "forward_ms": round(fwd, 4), "lse_allgather_ms": round(gat, 4),
+        "rescale_ms": round(resc, 4), "reduce_scatter_ms": round(rs, 4),
+        "collective_share": round((gat + rs) / tot, 4),
+        "merge_share": round((tot - fwd) / tot, 4),
+        "layout": "rank g: zigzag key chunks g and 2N-1-g of all 16 heads, all 131072 query "
+                  "rows; merge = all-gather of row log-sum-exp (fp32 [16, 131072]), one "
+                  "mfa_lse_rescale_sum kernel, NCCL reduce-scatter by query rows of fp32 "
+                  "[131072, 16, 128]; each rank ends with ceil(L/N) rows",
+        "parity": {"max_abs_diff_vs_single_gpu": round(dd.item(), 6), "ok": dd.item() <= 2e-2,
+                   "windows_per_rank": len(sample_windows(r0, r1))},
+    }
+
+
 def run_gpu(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -284,15 +428,22 @@ def run_gpu(args):
         if dist is not None:
             dist.barrier()
 
+    def max_over_ranks(x):
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
     call, host_in, flops, nbytes, desc = workload(args.config, dev, rank, world)
     strong = bool(desc.pop("strong", False))
     total_flops = desc.pop("total_flops", world * flops)
     dev_in = [t.to(dev) for t in host_in]
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream(dev)
+    last = []
 
     def step():
-        call(*dev_in)
+        last[:] = [call(*dev_in)]
 
     for _ in range(args.warmup):
         step()
@@ -303,11 +454,20 @@ def run_gpu(args):
         times = timed_steps(step, args.steps, flush, stream)
     torch.cuda.synchronize()
     barrier()
-    t = torch.tensor([sum(times)], device=dev, dtype=torch.float64)
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_step = t.item() / args.steps
+    ms_step = max_over_ranks(sum(times)) / args.steps
     value = total_flops / (ms_step * 1e-3) / 1e12
+
+    # parity: sampled row windows of this rank's output against a single-GPU forward of the
+    # same rows (exact restatement for bottom-right causal Lq == Lk)
+    parity = None
+    if args.config in ("5", "2", "target"):
+        L = desc["seq_len"]
+        diff = max_over_ranks(window_diff(*dev_in, last[0], sample_windows(0, L)))
+        parity = {"max_abs_diff_vs_single_gpu": round(diff, 6), "ok": diff <= 2e-2,
+                  "windows": [list(w) for w in sample_windows(0, L)],
+                  "what": "rows [r0, r1) of every head this rank ran vs a separate forward of "
+                          "Lq = r1 - r0 over keys [0, r1)"}
+    del last[:]
 
     # end-to-end through the public host-memory API (flash_attn_host): pinned host inputs in,
     # the output back in pinned host memory; the library overlaps the copies with the compute
@@ -324,11 +484,9 @@ def run_gpu(args):
     barrier()
     e_times = timed_steps(e2e_step, args.e2e_steps, flush, stream)
     torch.cuda.synchronize()
-    te = torch.tensor([sum(e_times)], device=dev, dtype=torch.float64)
-    if dist is not None:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = te.item() / args.e2e_steps
+    e2e_ms = max_over_ranks(sum(e_times)) / args.e2e_steps
     d2h = out_host.numel() * out_host.element_size()
+    del pinned, out_host, dev_in
 
     pk = peaks()
     achieved = flops / (statistics.mean(times) * 1e-3) / 1e12
@@ -340,47 +498,84 @@ def run_gpu(args):
                 traffic = json.load(f).get(desc["workload"])
         except Exception:
             traffic = None
+    launches = args.steps  # the main timed region: one forward kernel per step
+
+    split = None
+    if world > 1 and args.config == "5" and not args.no_split_kv:
+        torch.cuda.empty_cache()
+        split = split_kv_leg(min(args.steps, args.split_steps), args.warmup, dev, rank, world,
+                             flush, stream, dist)
+        torch.cuda.empty_cache()
+
+    configs = None
+    if world == 1 and not args.no_sub_configs:
+        configs = {}
+        for c in SUB_CONFIGS:
+            if c == args.config:
+                continue
+            torch.cuda.empty_cache()
+            n = min(args.steps, args.sub_steps)
+            t_c, f_c, b_c, d_c, *_ = measure(c, dev, n, args.warmup, flush, stream)
+            ms = statistics.mean(t_c)
+            tf = f_c / (ms * 1e-3) / 1e12
+            configs[d_c["workload"]] = {
+                "value": round(tf, 3), "unit": "TFLOP/s", "ms_per_step": round(ms, 5),
+                "steps": n, "frac_of_bf16_peak": round(tf / pk["bf16"], 4),
+                "config": d_c,
+                **({"note": "fp32 inputs: CUDA-core kernel, not a tensor-core rate"}
+                   if c == "1" else {}),
+            }
+
     line = None
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
-            "higher_is_better": True, "scaling": "strong" if strong else "weak",
+            "higher_is_better": True, "scaling": "strong" if strong or args.config == "5" else "weak",
             "vs_baseline": None,
             "dtype": desc.get("dtype", "bfloat16").replace("bfloat16", "bf16").replace(
-                "float16", "fp16"),
-            "data": "synthetic (seeded N(0,1), BASELINE shapes)",
-            "config": dict(desc, global_batch=(desc.get("batch_per_rank", 1) if strong else
-                                              world * desc.get("batch_per_rank", 1)),
+                "float16", "fp16").replace("float32", "f32"),
+            "data": "synthetic (seeded N(0,1) scaled as BASELINE states, BASELINE shapes)",
+            "config": dict(desc, global_batch=(desc.get("batch_per_rank", 1) if strong or world == 1
+                                              else world * desc.get("batch_per_rank", 1)),
                            parallelism=(f"heads{world} (one sequence, KV-group-aligned head "
                                         "shards, no collective)" if strong else
+                                        "single GPU" if world == 1 else
                                         f"dp{world} (batch shards, no collective)"),
-                           l2="flushed (256 MiB write) before every timed step"),
+                           l2="flushed (256 MiB write) before every timed step; inputs > L2"),
             "pct_of_peak": round(100 * value / world / pk["bf16"], 2),
             "hbm_gbs_compulsory": round(nbytes / (ms_step * 1e-3) / 1e9, 1),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 3),
                          "peak": pk["bf16"], "unit": "TFLOP/s",
                          "frac": round(achieved / pk["bf16"], 4),
                          "peak_source": f"bf16_tflops (burst) of {pk['source']} peaks",
+                         "frac_of_sustained": round(achieved / pk["bf16_sustained"], 4),
                          "traffic": traffic},
             "e2e": {"value": round(total_flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms, 4),
                     "api": "flash_attn_host / flash_attn_varlen_host (host tensors in and out; "
                            "copies of one piece overlap the forward of another)"},
-            "gpu_launches": args.steps,
+            "gpu_launches": launches,
             "clocks": clk.summary(),
         }
+        if parity is not None:
+            line["parity"] = parity
+        if split is not None:
+            line["split_kv"] = split
+        if configs is not None:
+            line["configs"] = configs
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             torch.set_num_threads(os.cpu_count() or 1)
-            tf, _, sdesc = cpu_sample_run(reps_budget_s=args.cpu_seconds)
+            tf, _, sdesc = cpu_sample_run(reps_budget_s=args.cpu_seconds, rows=256)
             line["cpu_baseline"] = {"value": round(tf, 6), "unit": "TFLOP/s",
                                     "cores": torch.get_num_threads(), "kind": "port",
-                                    "sample": sdesc}
+                                    "sample": sdesc,
+                                    "config1_full": cpu_config1_run()}
         print(json.dumps(line), flush=True)
     return 0
 
@@ -388,13 +583,17 @@ def run_gpu(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--e2e-steps", type=int, default=20)
-    ap.add_argument("--config", default="2", choices=["2", "3", "4", "5", "target"])
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--split-steps", type=int, default=10)
+    ap.add_argument("--sub-steps", type=int, default=30)
+    ap.add_argument("--config", default="5", choices=["1", "2", "3", "4", "5", "target"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-split-kv", action="store_true")
+    ap.add_argument("--no-sub-configs", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

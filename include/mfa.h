@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define MFA_ABI_VERSION 4
+#define MFA_ABI_VERSION 5
 
 /* Status codes. The Python layer maps them to the reference's exception types. */
 enum mfa_status {
@@ -67,7 +67,11 @@ typedef struct mfa_fwd_params {
   int32_t B, Hq, Hkv, Lq, Lk, D;
   /* varlen: device int32 [B+1] cumulative lengths, or NULL for dense. With varlen the batch
    * strides are ignored, rows are absolute token indices, Lq/Lk hold the total token counts
-   * (total_q, total_k) and max_lq must be >= every per-sequence query length. */
+   * (total_q, total_k) and max_lq must be >= every per-sequence query length. With a
+   * workspace (or mfa_fwd_noalloc) Lq must also be >= cu_q[B]: split partial rows are addressed
+   * by packed row, and a row at or past Lq is not stored but reported as MFA_ERR_INVALID in
+   * *err. A launch over some of the sequences of a larger packed batch touches only the rows
+   * [cu_q[0], cu_q[B]) of o and lse. */
   const int32_t* cu_q;
   const int32_t* cu_k;
   int32_t max_lq, max_lk;
@@ -84,7 +88,8 @@ typedef struct mfa_fwd_params {
   int32_t k_pos_offset;
   int32_t lk_total;
   int32_t kernel;      /* mfa_kernel */
-  int32_t* err;        /* optional device int; a kernel that times out stores MFA_ERR_TIMEOUT */
+  int32_t* err;        /* optional device int; a kernel that times out stores MFA_ERR_TIMEOUT,
+                          a split launch whose varlen rows pass Lq stores MFA_ERR_INVALID */
   /* Optional caller-owned device scratch for splitting the keys of one launch over several
    * CTAs when there are too few query rows to fill the GPU (decode-like Lq). Size it with
    * mfa_fwd_workspace_size; NULL or too small simply disables the split. */
@@ -108,7 +113,9 @@ int mfa_fwd(const mfa_fwd_params* p, void* cuda_stream);
  * need more than 16 MiB of that scratch is rejected with MFA_ERR_SCRATCH_TOO_SMALL (use
  * mfa_fwd with a workspace for it); problems that do not split need no scratch at all.
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
- * that device current; make that first call before any stream capture. All calls share the
+ * that device current; make that first call before any stream capture. The address is kept for
+ * the life of the process: do not use this entry point across a cudaDeviceReset (or any other
+ * teardown of the device's primary context), after which the kept address is stale. All calls share the
  * one array: calls whose kernels can overlap on the GPU (different streams, or several host
  * threads) race on it and must be serialised by the caller. Nothing in it needs to start at
  * zero: each call overwrites every slot it reads. */
@@ -141,6 +148,16 @@ int mfa_select_kernel(const mfa_fwd_params* p);
 int mfa_lse_combine(const float* const* o_part, const float* const* lse_part, int32_t n,
                     int32_t rows, int32_t H, int32_t D, void* o, int32_t o_dtype,
                     float* lse, void* cuda_stream);
+
+/* First half of a split-KV merge whose partials live on several GPUs (no counterpart in the
+ * reference). With o_part/lse_part laid out as in mfa_lse_combine and lse_ref fp32 [H, rows]
+ * the log-sum-exp of the row over every partial on every GPU, writes
+ * o[row, h, :] = sum_g exp(lse_g - lse_ref) o_g[row, h, :] (terms with lse_g or lse_ref = -inf
+ * are 0). Summing these over the GPUs (an NCCL reduce-scatter by query rows) gives the exact
+ * merged rows: the second half of the merge is the collective itself. */
+int mfa_lse_rescale_sum(const float* const* o_part, const float* const* lse_part, int32_t n,
+                        int32_t rows, int32_t H, int32_t D, const float* lse_ref, void* o,
+                        int32_t o_dtype, void* cuda_stream);
 
 /* Host buffers of mfa_fwd_staged. */
 typedef struct {

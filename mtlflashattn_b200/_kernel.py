@@ -117,7 +117,10 @@ def check_device_errors(device=None):
     v = int(t.item())
     if v != 0:
         t.zero_()
-        raise _lib.MfaError(v, "a kernel gave up on a bounded wait; its output is invalid")
+        why = ("a kernel gave up on a bounded wait" if v == _lib.ERR_TIMEOUT else
+               "a split launch met a varlen row at or past Lq (Lq < cu_seqlens[-1])"
+               if v == _lib.ERR_INVALID else "a kernel reported an error")
+        raise _lib.MfaError(v, why + "; its output is invalid")
 
 
 def _sync_check_enabled():

@@ -13,7 +13,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmfa.so")
 
-MFA_ABI_VERSION = 4
+MFA_ABI_VERSION = 5
 
 # mfa_status
 OK = 0
@@ -42,6 +42,7 @@ EXPORTED_SYMBOLS = (
     "mfa_fwd_packed_heads",
     "mfa_select_kernel",
     "mfa_lse_combine",
+    "mfa_lse_rescale_sum",
     "mfa_selftest_wait_timeout",
     "mfa_status_string",
     "mfa_abi_version",
@@ -151,6 +152,12 @@ def load(path: str | None = None) -> ctypes.CDLL:
             ctypes.c_void_p, ctypes.c_void_p,
         ]
         lib.mfa_lse_combine.restype = ctypes.c_int
+        lib.mfa_lse_rescale_sum.argtypes = [
+            ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32,
+            ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+            ctypes.c_int32, ctypes.c_void_p,
+        ]
+        lib.mfa_lse_rescale_sum.restype = ctypes.c_int
         lib.mfa_selftest_wait_timeout.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]
         lib.mfa_selftest_wait_timeout.restype = ctypes.c_int
         lib.mfa_status_string.argtypes = [ctypes.c_int]
@@ -206,3 +213,11 @@ def lse_combine(o_ptrs, lse_ptrs, rows, H, D, o_ptr, o_dtype, lse_ptr, stream) -
     la = (ctypes.c_void_p * n)(*lse_ptrs)
     return load().mfa_lse_combine(oa, la, n, rows, H, D, ctypes.c_void_p(o_ptr), o_dtype,
                                   ctypes.c_void_p(lse_ptr or 0), ctypes.c_void_p(stream))
+
+
+def lse_rescale_sum(o_ptrs, lse_ptrs, rows, H, D, lse_ref_ptr, o_ptr, o_dtype, stream) -> int:
+    n = len(o_ptrs)
+    oa = (ctypes.c_void_p * n)(*o_ptrs)
+    la = (ctypes.c_void_p * n)(*lse_ptrs)
+    return load().mfa_lse_rescale_sum(oa, la, n, rows, H, D, ctypes.c_void_p(lse_ref_ptr),
+                                      ctypes.c_void_p(o_ptr), o_dtype, ctypes.c_void_p(stream))

@@ -49,6 +49,8 @@ struct FwdArgs {
   // hk * 2^pack_shift + (r & (2^pack_shift - 1)); the 2^pack_shift heads of a KV group share
   // every K/V block load
   int pack_shift;
+  // sequences of a varlen launch (B before the split merge views the packed rows as one batch)
+  int nseq;
 };
 
 // One (batch, sequence) view after resolving dense vs varlen.

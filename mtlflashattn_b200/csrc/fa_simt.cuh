@@ -194,6 +194,66 @@ __global__ void lse_combine_kernel(const __grid_constant__ PartPtrs pp, int n, i
   if (lane == 0 && lse_out != nullptr) lse_out[li] = lse;
 }
 
+// Weighted sum of n split-KV partials against a log-sum-exp computed elsewhere (the first half
+// of a merge whose partials live on several GPUs): o = sum_g exp(lse_g - lse_ref) o_g, with a
+// term of 0 where lse_g or lse_ref is -inf. When lse_ref is the log-sum-exp of every partial of
+// the row on every GPU, the per-GPU sums add up (a reduce-scatter) to the exact merged row, so
+// no second pass over the output is needed. One warp per (row, head); each lane owns four
+// consecutive columns (16-byte loads) when D % 4 == 0 and every pointer is 16-byte aligned.
+template <typename TO>
+__global__ void lse_rescale_sum_kernel(const __grid_constant__ PartPtrs pp, int n, int rows,
+                                       int H, int D, const float* __restrict__ lse_ref, TO* o,
+                                       int vec4) {
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (int64_t)rows * H) return;
+  const int row = (int)(w / H), h = (int)(w % H);
+  const int64_t li = (int64_t)h * rows + row;
+  const int64_t oi = ((int64_t)row * H + h) * D;
+  const float ref = lse_ref[li];
+  float wg[kMaxParts];
+#pragma unroll 4
+  for (int g = 0; g < n; ++g) {
+    const float lg = pp.lse[g][li];
+    wg[g] = (lg == -INFINITY || ref == -INFINITY) ? 0.f : expf(lg - ref);
+  }
+  auto put = [&](int d, float v) {
+    if constexpr (sizeof(TO) == 4) {
+      o[oi + d] = v;
+    } else {
+      o[oi + d] = TO(v);
+    }
+  };
+  if (vec4) {
+    for (int c = 4 * lane; c < D; c += 128) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int g = 0; g < n; ++g) {
+        if (wg[g] == 0.f) continue;  // also skips partials that were never written (-inf rows)
+        const float4 x = *reinterpret_cast<const float4*>(pp.o[g] + oi + c);
+        acc.x = fmaf(wg[g], x.x, acc.x);
+        acc.y = fmaf(wg[g], x.y, acc.y);
+        acc.z = fmaf(wg[g], x.z, acc.z);
+        acc.w = fmaf(wg[g], x.w, acc.w);
+      }
+      if constexpr (sizeof(TO) == 4) {
+        *reinterpret_cast<float4*>(o + oi + c) = acc;
+      } else {
+        put(c, acc.x);
+        put(c + 1, acc.y);
+        put(c + 2, acc.z);
+        put(c + 3, acc.w);
+      }
+    }
+  } else {
+    for (int d = lane; d < D; d += 32) {
+      float acc = 0.f;
+      for (int g = 0; g < n; ++g)
+        if (wg[g] != 0.f) acc = fmaf(wg[g], pp.o[g][oi + d], acc);
+      put(d, acc);
+    }
+  }
+}
+
 // Merge of the key splits of one launch (dense layout): partial outputs ws_o fp32
 // [split][B][Lq][Hq][D] normalised by their own sums, row log-sum-exp ws_lse [split][B][Hq][Lq].
 // One block of kCombineThreads per (batch, head, row). The split weights exp(lse_s - max) are
@@ -233,6 +293,9 @@ __global__ void __launch_bounds__(kCombineThreads)
   const int row = (int)(w % a.Lq);
   const int bh = (int)(w / a.Lq);
   const int h = bh % a.Hq, b = bh / a.Hq;
+  // varlen: only the packed rows of this launch's sequences hold partials; a launch over some of
+  // the sequences of a larger packed batch leaves every other row (and its slots) alone
+  if (a.cu_q != nullptr && (row < a.cu_q[0] || row >= a.cu_q[a.nseq])) return;
   const int64_t li = ((int64_t)b * a.Hq + h) * a.Lq + row;
   const int64_t lstride = (int64_t)a.B * a.Hq * a.Lq;
   const int64_t ostride = lstride * a.D;

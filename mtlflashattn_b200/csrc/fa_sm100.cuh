@@ -706,7 +706,13 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
     }
     if (ok) {
       tc_fence_after();
-      const bool store = row < sv.lq;
+      bool store = row < sv.lq;
+      // a split launch's partial rows live in a workspace sized by Lq (varlen: total_q); a
+      // caller whose Lq understates cu_q[B] gets an error word instead of a write past its end
+      if (store && a.num_splits > 1 && sv.q0 + row >= a.Lq) {
+        store = false;
+        if (a.err != nullptr) atomicExch(a.err, 1 /*MFA_ERR_INVALID*/);
+      }
       const float inv = l > 0.f ? 1.f / l : 0.f;
       uint8_t* orow = nullptr;
       if (store) {

@@ -108,15 +108,33 @@ def test_sdpa_install_uninstall_and_cpu_passthrough(monkeypatch):
     assert not sdpa.install()
 
 
-def test_sdpa_uneven_v_shield_matches_direct():
-    q = torch.randn(1, 2, 20, 8)
-    k = torch.randn(1, 2, 24, 8)
-    v = torch.randn(1, 2, 24, 16)
-    out = sdpa._uneven_v_attention(q, k, v, None, False, None, q_chunk=7)
-    ref = torch.softmax(q @ k.transpose(-1, -2) / 8 ** 0.5, -1) @ v
-    torch.testing.assert_close(out, ref, atol=1e-5, rtol=1e-5)
-    with pytest.raises(ValueError, match="enable_gqa"):
-        sdpa._uneven_v_attention(torch.randn(1, 4, 5, 8), k, v, None, False, None)
+def test_sdpa_uneven_v_padding_is_exact(monkeypatch):
+    """A routed call whose value head dim differs from the query/key one runs on q/k/v
+    zero-padded to the larger dim and slices the output: exact, checked here with the oracle
+    standing in for the kernel."""
+    from oracle import flash_torch as ref
+
+    seen = []
+
+    def fake_forward(q, k, v, scale, causal):
+        seen.append(q.shape[-1])
+        return ref.attention_heads_second(q, k, v, scale, causal)
+
+    monkeypatch.setattr(sdpa, "flash_attn_forward", fake_forward)
+    g = torch.Generator().manual_seed(3)
+    for Dqk, Dv in ((40, 64), (64, 24), (100, 128)):
+        q = torch.randn(1, 2, 20, Dqk, generator=g)
+        k = torch.randn(1, 2, 24, Dqk, generator=g)
+        v = torch.randn(1, 2, 24, Dv, generator=g)
+        for causal in (False, True):
+            if causal:
+                k, v = k[:, :, :20], v[:, :, :20]
+            out = sdpa._engine(q, k, v, causal, None)
+            want = torch.softmax((q @ k.transpose(-1, -2)) / Dqk ** 0.5 + (
+                torch.full((20, k.shape[2]), float("-inf")).triu(1) if causal else 0), -1) @ v
+            assert out.shape == (1, 2, 20, Dv)
+            torch.testing.assert_close(out, want, atol=1e-5, rtol=1e-5)
+    assert all(d % 8 == 0 for d in seen)
 
 
 def test_trace_records_and_summarises(monkeypatch):

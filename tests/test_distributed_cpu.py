@@ -1,6 +1,7 @@
 """Multi-rank logic on CPU with gloo (world size 2 and 3): head sharding covers every head once,
-zigzag key ranges partition the keys with equal causal work, the split-KV log-sum-exp merge over
-ranks reproduces the unsplit oracle result, and a rank that leaves surfaces as an error."""
+zigzag key ranges partition the keys with equal causal work, the split-KV log-sum-exp merge
+(all-gather of the row log-sum-exp, rescale, reduce-scatter by query rows) gives every rank
+exactly its rows of the unsplit oracle result, and a rank that leaves surfaces as an error."""
 import os
 import socket
 
@@ -43,23 +44,35 @@ def _free_port():
     return p
 
 
+def cpu_rescale(o_parts, lse_parts, lse_ref, out):
+    """CPU statement of the library's mfa_lse_rescale_sum (the GPU kernel), for the host-logic
+    test: out[:Lq] = sum_g exp(lse_g - lse_ref) o_g, 0 where either is -inf."""
+    Lq = o_parts[0].shape[0]
+    acc = torch.zeros_like(o_parts[0])
+    for o, lse in zip(o_parts, lse_parts):
+        w = torch.exp(lse - lse_ref)
+        w = torch.where(torch.isinf(lse) | torch.isinf(lse_ref), torch.zeros_like(w), w)
+        acc += w.t()[..., None] * o
+    out[:Lq] = acc
+
+
 def _merge_worker(rank, world, port, q, k, v, causal, result_q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from oracle import flash_torch as ref
         L = k.shape[2]
-        parts = []
+        o_parts, lse_parts = [], []
         for a, b in mfd.zigzag_ranges(L, world, rank):
-            parts.append(ref.attention_heads_second(q, k[:, :, a:b], v[:, :, a:b], 0.2, causal,
-                                                    softcap=7.0, alibi=torch.tensor([0.1, 0.3]),
-                                                    return_lse=True, key_offset=a, lk_total=L))
-        lses = torch.stack([p[1] for p in parts])
-        lse_loc = torch.logsumexp(lses, 0)
-        w = torch.nan_to_num(torch.exp(lses - lse_loc), nan=0.0)
-        o_loc = sum(w[i][..., None] * parts[i][0] for i in range(len(parts)))
-        o, lse = mfd.merge_partials(o_loc.transpose(1, 2).contiguous(), lse_loc)
-        result_q.put((rank, o, lse))
+            o, lse = ref.attention_heads_second(q, k[:, :, a:b], v[:, :, a:b], 0.2, causal,
+                                                softcap=7.0, alibi=torch.tensor([0.1, 0.3]),
+                                                return_lse=True, key_offset=a, lk_total=L)
+            B, H, Lq, D = o.shape
+            # the forward's output strides put partial rows in [Lq, B*H, D]
+            o_parts.append(o.permute(2, 0, 1, 3).reshape(Lq, B * H, D).contiguous())
+            lse_parts.append(lse.reshape(B * H, Lq))
+        o, lse, rows = mfd.merge_partials(o_parts, lse_parts, rescale=cpu_rescale)
+        result_q.put((rank, o, lse, rows))
     finally:
         dist.destroy_process_group()
 
@@ -67,6 +80,8 @@ def _merge_worker(rank, world, port, q, k, v, causal, result_q):
 @pytest.mark.parametrize("world", [2, 3])
 @pytest.mark.parametrize("causal", [True, False])
 def test_split_kv_merge_over_gloo_matches_unsplit(world, causal):
+    """Each rank ends with exactly its own query rows of the merged output (reduce-scatter by
+    rows), equal to the unsplit oracle result; together the ranks cover every row once."""
     from oracle import flash_torch as ref
     q, k, v = ref.make_qkv(1, 50, 96, 2, 2, 16, torch.float32, seed=5)
     qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
@@ -83,10 +98,25 @@ def test_split_kv_merge_over_gloo_matches_unsplit(world, causal):
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for _, o, lse in results:
-        torch.testing.assert_close(o, full.transpose(1, 2), atol=1e-5, rtol=1e-5)
-        fin = torch.isfinite(full_lse)
-        torch.testing.assert_close(lse[fin], full_lse[fin], atol=1e-5, rtol=1e-5)
+    want = full[0].transpose(0, 1)  # [Lq, H, D]
+    covered = []
+    for rank, o, lse, (r0, r1) in results:
+        assert (r0, r1) == mfd.row_shard(50, world, rank)
+        covered += list(range(r0, r1))
+        torch.testing.assert_close(o, want[r0:r1], atol=1e-5, rtol=1e-5)
+        wl = full_lse[0][:, r0:r1]
+        fin = torch.isfinite(wl)
+        torch.testing.assert_close(lse[fin], wl[fin], atol=1e-5, rtol=1e-5)
+    assert sorted(covered) == list(range(50))
+
+
+def test_row_shard_partition():
+    for Lq in (1, 7, 50, 131072):
+        for world in (1, 2, 3, 8):
+            got = [mfd.row_shard(Lq, world, r) for r in range(world)]
+            assert got[0][0] == 0 and got[-1][1] == Lq
+            for (_, b), (c, _) in zip(got, got[1:]):
+                assert b == c
 
 
 def _dead_rank_worker(rank, world, port, result_q):
@@ -98,7 +128,7 @@ def _dead_rank_worker(rank, world, port, result_q):
                                 timeout=datetime.timedelta(seconds=5))
         if rank == 1:
             os._exit(0)
-        mfd.merge_partials(torch.zeros(1, 4, 2, 8), torch.zeros(1, 2, 4))
+        mfd.merge_partials([torch.zeros(4, 2, 8)], [torch.zeros(2, 4)], rescale=cpu_rescale)
         result_q.put("no-error")
     except Exception as e:  # noqa: BLE001 - init or the collective saw the missing rank
         if rank == 0:

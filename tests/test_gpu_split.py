@@ -140,3 +140,69 @@ def test_varlen_split_row_lse_and_understated_max_lk():
                                                v[ks].permute(1, 0, 2)[None], scale, True,
                                                return_lse=True)
             torch.testing.assert_close(lse[:, qs].cpu(), wl[0], atol=1e-3, rtol=1e-4)
+
+
+def _varlen_params(q, k, v, o, cu_q, cu_k, max_lq, max_lk, lse=None):
+    return _kernel._params(q, k, v, o, B=cu_q.shape[0] - 1, Hq=q.shape[1], Hkv=k.shape[1],
+                           Lq=q.shape[0], Lk=k.shape[0], D=q.shape[2],
+                           q_st=(0, q.stride(0), q.stride(1)), k_st=(0, k.stride(0), k.stride(1)),
+                           v_st=(0, v.stride(0), v.stride(1)), o_st=(0, o.stride(0), o.stride(1)),
+                           scale=1 / math.sqrt(q.shape[2]), causal=True,
+                           bias=_kernel._BiasParams(0.0, -1, -1, None), kernel=_lib.KERNEL_AUTO,
+                           lse=lse, lse_st=((0, lse.stride(0)) if lse is not None else (0, 0)),
+                           cu_q=cu_q, cu_k=cu_k, max_lq=max_lq, max_lk=max_lk)
+
+
+def test_varlen_split_over_part_of_a_batch_leaves_other_rows_alone():
+    """Two split launches, each over half of the sequences of one packed batch, into the same
+    output through the same (dirty) workspace: each writes only its own packed rows, and
+    together they give the whole batch's result."""
+    lq, lk = [1, 2, 1, 3], [12000, 9000, 15000, 7000]
+    Hq, Hkv, D = 16, 4, 128
+    q, k, v, cu_q, cu_k = ref.make_varlen(lq, lk, Hq, Hkv, D, torch.bfloat16, seed=33)
+    qd, kd, vd, cqd, ckd = (t.to(DEV) for t in (q, k, v, cu_q, cu_k))
+    want = ref.flash_attn_varlen_func(q, k, v, cu_q, cu_k, causal=True)
+    sentinel = 123.0
+    o = torch.full_like(qd, sentinel)
+    lse = torch.full((Hq, q.shape[0]), sentinel, device=DEV, dtype=torch.float32)
+    stream = torch.cuda.current_stream().cuda_stream
+    ws = torch.full((64 << 20,), 0x7F, dtype=torch.uint8, device=DEV)  # stale, non-zero bytes
+    halves = [(0, 2), (2, 4)]
+    for n, (s0, s1) in enumerate(halves):
+        p = _varlen_params(qd, kd, vd, o, cqd[s0:s1 + 1], ckd[s0:s1 + 1], max(lq), max(lk), lse)
+        need = _lib.workspace_size(p)
+        assert 0 < need <= ws.numel()
+        p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+        assert _lib.num_splits(p) > 1
+        assert _lib.fwd(p, stream) == _lib.OK
+        torch.cuda.synchronize()
+        r0, r1 = int(cu_q[s0]), int(cu_q[s1])
+        # rows of sequences not yet run are untouched
+        later = int(cu_q[halves[n][1]])
+        assert torch.all(o[later:] == sentinel)
+        assert torch.all(lse[:, later:] == sentinel)
+        torch.testing.assert_close(o[r0:r1].float().cpu(), want[r0:r1], **TOL[torch.bfloat16])
+    torch.testing.assert_close(o.float().cpu(), want, **TOL[torch.bfloat16])
+    _kernel.check_device_errors(DEV)
+
+
+def test_varlen_split_with_understated_lq_reports_instead_of_writing_past_workspace():
+    """A C caller whose Lq (total_q) is below cu_q[B] gets MFA_ERR_INVALID in the error word;
+    the rows past Lq are not stored into the workspace."""
+    lq, lk = [1, 1, 2], [12000, 9000, 15000]
+    Hq, Hkv, D = 8, 2, 128
+    q, k, v, cu_q, cu_k = ref.make_varlen(lq, lk, Hq, Hkv, D, torch.bfloat16, seed=34)
+    qd, kd, vd, cqd, ckd = (t.to(DEV) for t in (q, k, v, cu_q, cu_k))
+    o = torch.zeros_like(qd)
+    p = _varlen_params(qd, kd, vd, o, cqd, ckd, max(lq), max(lk))
+    p.Lq = q.shape[0] - 2  # understated total_q
+    need = _lib.workspace_size(p)
+    ws = torch.zeros(need + (1 << 20), dtype=torch.uint8, device=DEV)
+    guard = ws[need:].clone()
+    p.workspace, p.workspace_bytes = ws.data_ptr(), need
+    assert _lib.num_splits(p) > 1
+    assert _lib.fwd(p, torch.cuda.current_stream().cuda_stream) == _lib.OK
+    with pytest.raises(_lib.MfaError) as ei:
+        _kernel.check_device_errors(DEV)
+    assert ei.value.status == _lib.ERR_INVALID
+    assert torch.equal(ws[need:], guard)  # nothing written past the planned workspace

@@ -66,7 +66,7 @@ def test_sdpa_stock_fallbacks_are_bitwise(patched):
                        patched._orig(q, k, v, is_causal=True))
 
 
-def test_sdpa_gates():
+def test_sdpa_gates(monkeypatch):
     assert sdpa.install()
     try:
         q, k, v = bhld(1, 2, 64, 64, 64)
@@ -75,22 +75,57 @@ def test_sdpa_gates():
         q, k, v = bhld(1, 4, 2048, 2048, 64)
         ok, reason = sdpa._eligibility(q, k, v, None, 0.0, False)
         assert ok and reason == "fast-tier"
+        # stock SDPA is exact on CUDA and faster than the CUDA-core kernel: a long call the
+        # tensor-core kernel cannot take stays on stock unless the all-tier floor is set
         q, k, v = bhld(1, 1, 4096, 4096, 100)
         ok, reason = sdpa._eligibility(q, k, v, None, 0.0, False)
+        assert not ok and reason.startswith("fits")
+    finally:
+        sdpa.uninstall()
+    monkeypatch.setenv("MTLFLASHATTN_SDPA_MIN_SEQ", "256")
+    assert sdpa.install()
+    try:
+        q, k, v = bhld(1, 1, 512, 512, 100)
+        ok, reason = sdpa._eligibility(q, k, v, None, 0.0, False)
         assert ok and reason == "correctness-large-seq"
+    finally:
+        sdpa.uninstall()
+    monkeypatch.setenv("MTLFLASHATTN_SDPA_FAST_MIN_SEQ", "256")
+    assert sdpa.install()
+    try:
+        q, k, v = bhld(1, 2, 512, 512, 64)
+        ok, reason = sdpa._eligibility(q, k, v, None, 0.0, False)
+        assert ok and reason == "fast-tier"
     finally:
         sdpa.uninstall()
 
 
 def test_sdpa_uneven_v(patched):
+    # fp32: routed by the memory gate (installed with a tiny budget), padded to D = 128
     q, k, v = bhld(1, 4, 128, 128, 64, dtype=torch.float32, Dv=128)
     out = F.scaled_dot_product_attention(q, k, v)
     assert out.shape == (1, 4, 128, 128)
     want = torch.softmax(q.cpu() @ k.cpu().transpose(-1, -2) / 8.0, -1) @ v.cpu()
     torch.testing.assert_close(out.cpu(), want, atol=2e-5, rtol=1e-4)
-    with pytest.raises(ValueError, match="enable_gqa"):
-        q, k, v = bhld(1, 8, 32, 32, 64, dtype=torch.float32, Hkv=2, Dv=128)
+    # bf16, value narrower than query/key, causal: the tensor-core kernel on padded inputs
+    q, k, v = bhld(1, 4, 300, 300, 128, dtype=torch.bfloat16, Dv=48)
+    out = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+    assert out.shape == (1, 4, 300, 48)
+    want = ref.attention_heads_second(q.float().cpu(), k.float().cpu(), v.float().cpu(),
+                                      1 / math.sqrt(128), True)
+    torch.testing.assert_close(out.float().cpu(), want, atol=2e-2, rtol=2e-2)
+    # GQA without enable_gqa is not routed: stock SDPA decides (and refuses it)
+    q, k, v = bhld(1, 8, 32, 32, 64, dtype=torch.float32, Hkv=2, Dv=128)
+    ok, reason = sdpa._decide(q, k, v, None, 0.0, False, enable_gqa=False)
+    assert not ok and reason.startswith("heads")
+    with pytest.raises(Exception):
         F.scaled_dot_product_attention(q, k, v)
+
+
+def test_sdpa_calibrate_runs():
+    rows, floor = sdpa.calibrate(lengths=(256, 1024), dims=(64,), causal=(True,), iters=2)
+    assert len(rows) == 2 and all(r["engine_ms"] > 0 and r["stock_ms"] > 0 for r in rows)
+    assert floor in (None, 256, 1024)
 
 
 def test_shim_serves_engine_functions():
@@ -135,9 +170,39 @@ def test_split_kv_single_rank_equals_unsplit(nccl_single_rank):
     q, k, v = ref.make_qkv(1, 700, 1000, 4, 4, 128, torch.bfloat16, seed=12)
     qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
     ranges = [(0, 300), (300, 1000)]
-    out = mfd.flash_attn_split_kv(qd, [kd[:, a:b] for a, b in ranges],
-                                  [vd[:, a:b] for a, b in ranges], ranges, 1000, causal=True,
-                                  softcap=20.0, alibi_slopes=torch.tensor([0.1] * 4, device=DEV))
+    out, rows = mfd.flash_attn_split_kv(qd, [kd[:, a:b] for a, b in ranges],
+                                        [vd[:, a:b] for a, b in ranges], ranges, 1000,
+                                        causal=True, softcap=20.0,
+                                        alibi_slopes=torch.tensor([0.1] * 4, device=DEV))
+    assert rows == (0, 700)
     want = ref.flash_attn_func(q, k, v, causal=True, softcap=20.0,
                                alibi_slopes=torch.tensor([0.1] * 4))
     torch.testing.assert_close(out.float().cpu(), want, atol=2e-2, rtol=2e-2)
+
+
+def test_lse_rescale_sum_kernel_matches_torch():
+    """mfa_lse_rescale_sum (the per-GPU half of the multi-GPU merge) against its statement in
+    torch, including -inf rows, an unaligned output (scalar path) and a bf16 output."""
+    from mtlflashattn_b200 import _lib
+    g = torch.Generator(device=DEV).manual_seed(5)
+    rows, H, D, n = 300, 6, 128, 3
+    o = [torch.randn(rows, H, D, device=DEV, generator=g) for _ in range(n)]
+    lse = [torch.randn(H, rows, device=DEV, generator=g) * 3 for _ in range(n)]
+    lse[1][2, :50] = float("-inf")
+    ref_lse = torch.logsumexp(torch.stack(lse), 0) + 0.25  # another GPU's share: +log(1.28)
+    ref_lse[0, :7] = float("-inf")
+    want = torch.zeros(rows, H, D, device=DEV)
+    for og, lg in zip(o, lse):
+        w = torch.exp(lg - ref_lse).nan_to_num(0.0)
+        w[torch.isinf(lg) | torch.isinf(ref_lse)] = 0
+        want += w.t()[..., None] * og
+    st = torch.cuda.current_stream().cuda_stream
+    for dt, code, off in ((torch.float32, _lib.FP32, 0), (torch.float32, _lib.FP32, 1),
+                          (torch.bfloat16, _lib.BF16, 0)):
+        buf = torch.empty(rows * H * D + off, device=DEV, dtype=dt)
+        out = buf[off:].view(rows, H, D)
+        rc = _lib.lse_rescale_sum([t.data_ptr() for t in o], [t.data_ptr() for t in lse], rows,
+                                  H, D, ref_lse.data_ptr(), out.data_ptr(), code, st)
+        assert rc == _lib.OK
+        torch.testing.assert_close(out.float(), want, atol=1e-5 if dt == torch.float32 else 2e-2,
+                                   rtol=1e-5 if dt == torch.float32 else 1e-2)

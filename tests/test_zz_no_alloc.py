@@ -68,3 +68,38 @@ def test_noalloc_refuses_problems_beyond_its_scratch():
     rc = _lib.fwd_noalloc(p, torch.cuda.current_stream().cuda_stream)
     assert rc == _lib.ERR_SCRATCH_TOO_SMALL
     assert "16 MiB" in _lib.status_string(rc)
+
+
+def varlen_params(q, k, v, o, cu_q, cu_k, max_lq, max_lk):
+    return _kernel._params(q, k, v, o, B=cu_q.shape[0] - 1, Hq=q.shape[1], Hkv=k.shape[1],
+                           Lq=q.shape[0], Lk=k.shape[0], D=q.shape[2],
+                           q_st=(0, q.stride(0), q.stride(1)), k_st=(0, k.stride(0), k.stride(1)),
+                           v_st=(0, v.stride(0), v.stride(1)), o_st=(0, o.stride(0), o.stride(1)),
+                           scale=1 / math.sqrt(q.shape[2]), causal=True,
+                           bias=_kernel._BiasParams(0.0, -1, -1, None), kernel=_lib.KERNEL_AUTO,
+                           cu_q=cu_q, cu_k=cu_k, max_lq=max_lq, max_lk=max_lk)
+
+
+def test_noalloc_varlen_split_two_calls_with_different_sequences():
+    """Batched decode through the varlen path: two no-allocation calls in a row with different
+    cu_seqlens share the scratch; each must match mfa_fwd with its own workspace (stale partials
+    of the first call must not leak into the second)."""
+    stream = torch.cuda.current_stream().cuda_stream
+    for seed, lq, lk in ((1, [1, 2, 1, 1], [9000, 15000, 300, 20000]),
+                         (2, [3, 1, 1], [4000, 22000, 11000])):
+        q, k, v, cu_q, cu_k = ref.make_varlen(lq, lk, 16, 4, 128, torch.bfloat16, seed=seed)
+        qd, kd, vd, cqd, ckd = (t.to(DEV) for t in (q, k, v, cu_q, cu_k))
+        o_ref = torch.empty_like(qd)
+        p = varlen_params(qd, kd, vd, o_ref, cqd, ckd, max(lq), max(lk))
+        need = _lib.workspace_size(p)
+        assert 0 < need <= 16 << 20, need
+        ws = torch.empty(need, dtype=torch.uint8, device=DEV)
+        p.workspace, p.workspace_bytes = ws.data_ptr(), need
+        assert _lib.num_splits(p) > 1
+        assert _lib.fwd(p, stream) == _lib.OK
+        o = torch.empty_like(qd)
+        assert _lib.fwd_noalloc(varlen_params(qd, kd, vd, o, cqd, ckd, max(lq), max(lk)),
+                                stream) == _lib.OK
+        torch.cuda.synchronize()
+        torch.testing.assert_close(o.float(), o_ref.float(), **TOL[torch.bfloat16])
+    _kernel.check_device_errors(DEV)
