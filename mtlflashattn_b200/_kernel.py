@@ -18,8 +18,11 @@ The reference's ``torch`` tier is not part of this engine: that chunked-fp32 alg
 from __future__ import annotations
 
 import atexit
+import ctypes
 import os
+import struct
 import sys
+import threading
 from collections import namedtuple
 
 import torch
@@ -109,7 +112,9 @@ def _err_word(device):
 
 def check_device_errors(device=None):
     """Synchronise and raise if any kernel on ``device`` reported a bounded-wait timeout."""
-    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    dev = torch.device(device) if device is not None else torch.device("cuda")
+    if dev.index is None:  # "cuda" names the current device; the words are keyed by index
+        dev = torch.device("cuda", torch.cuda.current_device())
     t = _err_words.get(dev)
     if t is None:
         return
@@ -154,37 +159,53 @@ def _raise_status(rc, what):
     raise _lib.MfaError(rc, what)
 
 
+_PACK = struct.Struct(_lib.PARAMS_FORMAT)
+_WS = struct.Struct("<QQ")
+_tls = threading.local()
+
+
+def _values(q, k, v, o, B, Hq, Hkv, Lq, Lk, D, q_st, k_st, v_st, o_st, scale, causal, bias,
+            kernel, lse, lse_st, cu_q, cu_k, max_lq, max_lk, k_pos_offset, lk_total):
+    """The fields of ``struct mfa_fwd_params`` in declaration order (workspace left empty)."""
+    return (q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+            lse.data_ptr() if lse is not None else 0,
+            *q_st, *k_st, *v_st, *o_st, *lse_st,
+            B, Hq, Hkv, Lq, Lk, D,
+            cu_q.data_ptr() if cu_q is not None else 0,
+            cu_k.data_ptr() if cu_k is not None else 0,
+            max_lq, max_lk, float(scale), float(bias.softcap), 1 if causal else 0,
+            int(bias.window_left), int(bias.window_right),
+            bias.alibi.data_ptr() if bias.alibi is not None else 0,
+            _DTYPES[q.dtype], _DTYPES[o.dtype], int(k_pos_offset), int(lk_total), kernel,
+            _err_word(q.device).data_ptr(), 0, 0)
+
+
 def _params(q, k, v, o, *, B, Hq, Hkv, Lq, Lk, D, q_st, k_st, v_st, o_st, scale, causal,
             bias: _BiasParams, kernel, lse=None, lse_st=(0, 0), cu_q=None, cu_k=None,
             max_lq=0, max_lk=0, k_pos_offset=0, lk_total=0):
-    p = _lib.MfaFwdParams()
-    p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
-    p.lse = lse.data_ptr() if lse is not None else None
-    p.q_stride[:] = q_st
-    p.k_stride[:] = k_st
-    p.v_stride[:] = v_st
-    p.o_stride[:] = o_st
-    p.lse_stride[:] = lse_st
-    p.B, p.Hq, p.Hkv, p.Lq, p.Lk, p.D = B, Hq, Hkv, Lq, Lk, D
-    p.cu_q = cu_q.data_ptr() if cu_q is not None else None
-    p.cu_k = cu_k.data_ptr() if cu_k is not None else None
-    p.max_lq, p.max_lk = max_lq, max_lk
-    p.scale = float(scale)
-    p.softcap = float(bias.softcap)
-    p.causal = 1 if causal else 0
-    p.win_left, p.win_right = int(bias.window_left), int(bias.window_right)
-    p.alibi = bias.alibi.data_ptr() if bias.alibi is not None else None
-    p.dtype = _DTYPES[q.dtype]
-    p.o_dtype = _DTYPES[o.dtype]
-    p.k_pos_offset = int(k_pos_offset)
-    p.lk_total = int(lk_total)
-    p.kernel = kernel
-    p.err = _err_word(q.device).data_ptr()
-    return p
+    """An ``MfaFwdParams`` (ctypes) for these tensors: for callers that inspect or edit fields
+    (the host-staged path, the plan queries, tests). The forward itself uses ``_packed``."""
+    vals = _values(q, k, v, o, B, Hq, Hkv, Lq, Lk, D, q_st, k_st, v_st, o_st, scale, causal,
+                   bias, kernel, lse, lse_st, cu_q, cu_k, max_lq, max_lk, k_pos_offset, lk_total)
+    return _lib.MfaFwdParams.from_buffer_copy(_PACK.pack(*vals))
 
 
-def _run(p, q, what, causal, trace_shape):
-    with torch.cuda.device(q.device):
+def _packed(*args):
+    """The same params packed into this thread's reusable buffer (valid until the next call on
+    this thread; libmfa reads it only during the call)."""
+    buf = getattr(_tls, "buf", None)
+    if buf is None:
+        buf = _tls.buf = ctypes.create_string_buffer(_PACK.size)
+    _PACK.pack_into(buf, 0, *_values(*args))
+    return buf
+
+
+def _run(p, q, what, causal, trace_shape, kernel, D):
+    dev = q.device
+    ctx = torch.cuda.device(dev) if dev.index != torch.cuda.current_device() else None
+    if ctx is not None:
+        ctx.__enter__()
+    try:
         if _trace_enabled():
             sel = _lib.select_kernel(p)
             label = "cuda/" + _lib.KERNEL_NAMES.get(sel, "rejected")
@@ -192,20 +213,23 @@ def _run(p, q, what, causal, trace_shape):
         ws = None
         need = _lib.workspace_size(p)
         if need > 0:  # few query rows: let the library split the keys over more CTAs
-            ws = torch.empty(need, dtype=torch.uint8, device=q.device)
-            p.workspace, p.workspace_bytes = ws.data_ptr(), need
-        rc = _lib.fwd(p, torch.cuda.current_stream(q.device).cuda_stream)
+            ws = torch.empty(need, dtype=torch.uint8, device=dev)
+            _WS.pack_into(p, _lib.WORKSPACE_OFFSET, ws.data_ptr(), need)
+        rc = _lib.fwd(p, torch.cuda.current_stream(dev).cuda_stream)
         del ws  # the caching allocator keeps it alive for work already queued on this stream
         if rc != _lib.OK:
-            if rc == _lib.ERR_UNSUPPORTED and p.kernel != _lib.KERNEL_AUTO:
+            if rc == _lib.ERR_UNSUPPORTED and kernel != _lib.KERNEL_AUTO:
                 raise RuntimeError(
-                    f"mtlflashattn_b200: {_lib.KERNEL_NAMES.get(p.kernel)} kernel forced but "
-                    f"ineligible (dtype={q.dtype}, D={p.D}; needs fp16/bf16, D%8==0, "
+                    f"mtlflashattn_b200: {_lib.KERNEL_NAMES.get(kernel)} kernel forced but "
+                    f"ineligible (dtype={q.dtype}, D={D}; needs fp16/bf16, D%8==0, "
                     f"16-byte aligned strides, sm_100 device)"
                 )
             _raise_status(rc, what)
+    finally:
+        if ctx is not None:
+            ctx.__exit__(None, None, None)
     if _sync_check_enabled():
-        check_device_errors(q.device)
+        check_device_errors(dev)
 
 
 def _check_tensors(q, k, v):
@@ -232,15 +256,12 @@ def forward_bshd(q, k, v, out, scale, causal, bias: _BiasParams, lse=None, k_pos
         raise NotImplementedError(f"mtlflashattn_b200: head_dim {D} > {MAX_HEAD_DIM}")
     if out.stride(-1) != 1:
         raise ValueError("mtlflashattn_b200: out must have a contiguous last dimension")
-    p = _params(q, k, v, out, B=B, Hq=Hq, Hkv=Hkv, Lq=Lq, Lk=Lk, D=D,
-                q_st=(q.stride(0), q.stride(1), q.stride(2)),
-                k_st=(k.stride(0), k.stride(1), k.stride(2)),
-                v_st=(v.stride(0), v.stride(1), v.stride(2)),
-                o_st=(out.stride(0), out.stride(1), out.stride(2)),
-                scale=scale, causal=causal, bias=bias, kernel=_tier_mode(q.dtype),
-                lse=lse, lse_st=((lse.stride(0), lse.stride(1)) if lse is not None else (0, 0)),
-                k_pos_offset=k_pos_offset, lk_total=lk_total)
-    _run(p, q, "flash_attn_forward", causal, (D, Lq, Lk))
+    kernel = _tier_mode(q.dtype)
+    p = _packed(q, k, v, out, B, Hq, Hkv, Lq, Lk, D, q.stride()[:3], k.stride()[:3],
+                v.stride()[:3], out.stride()[:3], scale, causal, bias, kernel, lse,
+                lse.stride()[:2] if lse is not None else (0, 0), None, None, 0, 0,
+                k_pos_offset, lk_total)
+    _run(p, q, "flash_attn_forward", causal, (D, Lq, Lk), kernel, D)
     return out
 
 
@@ -254,13 +275,13 @@ def forward_varlen(q, k, v, out, cu_q, cu_k, max_lq, max_lk, scale, causal, bias
     total_q, Hq, D = q.shape
     total_k, Hkv = k.shape[0], k.shape[1]
     batch = cu_q.shape[0] - 1
-    p = _params(q, k, v, out, B=batch, Hq=Hq, Hkv=Hkv, Lq=total_q, Lk=total_k, D=D,
-                q_st=(0, q.stride(0), q.stride(1)), k_st=(0, k.stride(0), k.stride(1)),
-                v_st=(0, v.stride(0), v.stride(1)), o_st=(0, out.stride(0), out.stride(1)),
-                scale=scale, causal=causal, bias=bias, kernel=_tier_mode(q.dtype),
-                lse=lse, lse_st=((0, lse.stride(0)) if lse is not None else (0, 0)),
-                cu_q=cu_q, cu_k=cu_k, max_lq=max_lq, max_lk=max_lk)
-    _run(p, q, "flash_attn_varlen_func", causal, (D, max_lq, max_lk))
+    kernel = _tier_mode(q.dtype)
+    p = _packed(q, k, v, out, batch, Hq, Hkv, total_q, total_k, D, (0, q.stride(0), q.stride(1)),
+                (0, k.stride(0), k.stride(1)), (0, v.stride(0), v.stride(1)),
+                (0, out.stride(0), out.stride(1)), scale, causal, bias, kernel, lse,
+                (0, lse.stride(0)) if lse is not None else (0, 0), cu_q, cu_k, max_lq, max_lk,
+                0, 0)
+    _run(p, q, "flash_attn_varlen_func", causal, (D, max_lq, max_lk), kernel, D)
     return out
 
 

@@ -38,11 +38,15 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(s) <= t for s in sources())
 
 
-def build(verbose: bool = False, force: bool = False) -> str:
-    if not force and up_to_date():
+def build(verbose: bool = False, force: bool = False, defines=(), out: str | None = None) -> str:
+    """Compile libmfa.so (or, with ``out``, a variant of it at that path; ``defines`` are
+    extra NAME=VALUE macros, e.g. the tuning knobs at the top of csrc/fa_sm100.cuh)."""
+    target = out or OUT
+    if not force and out is None and not defines and up_to_date():
         return OUT
     cmd = [nvcc_path(), *ARCH, "-O3", "-std=c++17", "-lineinfo", "--use_fast_math",
-           "-Xcompiler", "-fPIC", "-shared", "-o", OUT + ".tmp", SRC]
+           "-Xcompiler", "-fPIC", "-shared", *[f"-D{d}" for d in defines], "-o", target + ".tmp",
+           SRC]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     r = subprocess.run(cmd, capture_output=True, text=True)
@@ -50,8 +54,8 @@ def build(verbose: bool = False, force: bool = False) -> str:
         raise RuntimeError("nvcc failed:\n" + r.stdout + r.stderr)
     if verbose:
         sys.stderr.write(r.stdout + r.stderr)
-    os.replace(OUT + ".tmp", OUT)
-    return OUT
+    os.replace(target + ".tmp", target)
+    return target
 
 
 if __name__ == "__main__":

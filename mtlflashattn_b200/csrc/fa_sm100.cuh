@@ -122,6 +122,16 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 #ifndef MFA_EMU128
 #define MFA_EMU128 0
 #endif
+// The same for the softcap kernel (kBias = 2), whose three MUFU operations per score (two ex2
+// and a reciprocal, or an ex2 and a tanh) make it MUFU-bound.
+#ifndef MFA_EMU_SOFTCAP
+#define MFA_EMU_SOFTCAP 0
+#endif
+// Softcap tanh: 0 = 1 - 2 / (2^(2 y log2e) + 1) with MUFU ex2 and rcp (or Newton); 1 = the
+// hardware tanh.approx (one MUFU operation instead of two).
+#ifndef MFA_SOFTCAP_TANH
+#define MFA_SOFTCAP_TANH 0
+#endif
 // Score transform, a template parameter of the kernel:
 //   kBias = 0  x = s                        (c = scale*log2e folded into the exponent)
 //   kBias = 1  x = log2e*(s*scale - slope*|centre - key|)   (any scale, ALiBi optional)
@@ -185,7 +195,8 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
 // the other instantiations fold pack_shift to 0 at compile time.
 template <int DP, bool kBF16, int kBias, int CG = DefaultCG<kBias>::value,
           int TILES = DefaultTiles<DP, CG>::value, bool kPack = false,
-          int kEmu = (DP == 64 ? (TILES == 1 ? MFA_EMU64 : 0) : MFA_EMU128)>
+          int kEmu = (kBias == 2 ? MFA_EMU_SOFTCAP
+                                 : DP == 64 ? (TILES == 1 ? MFA_EMU64 : 0) : MFA_EMU128)>
 __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
                                   sm100::Roles<CG, TILES>::kCtasPerSm)
     fa_fwd_sm100(const __grid_constant__ Sm100Args args) {
@@ -486,6 +497,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
     // softcap: x = cap*log2e*tanh(y) with tanh(y) = 1 - 2/(2^(2*log2e*y) + 1), y = s*scale/cap
     const float sc_in = cap > 0.f ? a.scale * 2.f * kLog2e / cap : 0.f;
     const float sc_a = cap * kLog2e, sc_b = -2.f * cap * kLog2e;
+    const float sc_tin = cap > 0.f ? a.scale / cap : 0.f;  // hardware tanh: y = s*scale/cap
     const float pl_scale = a.scale * kLog2e;  // no softcap: x = s*scale*log2e
     const float centre = (float)(row + sv.off);
     // partner exchange slots: xch[parity][t][cg][row]
@@ -551,7 +563,11 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
         for (int i = 0; i < NC; i += 2) {
           uint64_t s2 = f2pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
           uint64_t x2;
-          if constexpr (kBias == 2) {
+          if constexpr (kBias == 2 && MFA_SOFTCAP_TANH) {
+            float ya, yb;
+            f2unpack(fmul2(s2, f2pack(sc_tin, sc_tin)), ya, yb);
+            x2 = fmul2(f2pack(tanh_hw(ya), tanh_hw(yb)), f2pack(sc_a, sc_a));
+          } else if constexpr (kBias == 2) {
             float ya, yb;
             f2unpack(fmul2(s2, f2pack(sc_in, sc_in)), ya, yb);
             // no clamp needed: 2^y overflows to +inf -> rcp = 0 -> tanh = 1; 2^y -> 0 -> tanh = -1

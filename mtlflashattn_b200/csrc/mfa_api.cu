@@ -365,6 +365,11 @@ int sm100_tiles_rt(bool wide, int gen) {
   return gen == 2 ? sm100_tiles<64, 2>() : gen == 1 ? sm100_tiles<64, 1>() : sm100_tiles<64, 0>();
 }
 
+// K/V bytes of the (batch, head) pairs whose CTAs run together (see run_sm100).
+#ifndef MFA_L2_GROUP_MB
+#define MFA_L2_GROUP_MB 64
+#endif
+
 // SHORT: the one-tile, one-column-group kPack instantiation (sm100_short).
 template <int DP, bool BF16, int GEN, bool SHORT>
 int launch_sm100(const Sm100Args& args, int dev, int64_t grid, cudaStream_t st) {
@@ -444,7 +449,7 @@ int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
     // K/V bytes of one KV head of one sequence; groups of whole KV groups whose K/V stays
     // within ~64 MB of L2 (all of them when everything fits)
     const int64_t kv_unit = (int64_t)(varlen ? p->max_lk : p->Lk) * p->D * 2 * 2;
-    int64_t units = kv_unit > 0 ? (64ll << 20) / kv_unit : (1ll << 30);
+    int64_t units = kv_unit > 0 ? ((int64_t)MFA_L2_GROUP_MB << 20) / kv_unit : (1ll << 30);
     if (units < 1) units = 1;
     const int64_t all = (int64_t)heads * a.B;
     const int64_t ghb = units * (p->Hq / p->Hkv >> a.pack_shift);

@@ -14,8 +14,8 @@ reason to route a call is that this engine is faster on it, and the only safety 
 the memory one:
 
 * ``fast-tier``: the tcgen05 kernel would run the call (fp16/bf16, D % 8 == 0, aligned) and
-  max(Lq, Lk) >= ``fast_min_seq``. The default is the crossover measured by ``calibrate()`` on
-  B200 against stock SDPA with its default backend choice.
+  max(Lq, Lk) >= ``fast_min_seq``. The default comes from ``calibrate()`` on B200 against stock
+  SDPA with its default backend choice (see DEFAULT_FAST_MIN_SEQ).
 * ``correctness-large-seq``: kept as the name of a length floor that routes every tier,
   including the fp32 CUDA-core kernel. Stock SDPA is not wrong on CUDA, and the CUDA-core
   kernel is slower than stock's fused fp32 path, so by default this floor is off; setting
@@ -43,9 +43,12 @@ from ._kernel import MAX_HEAD_DIM, _select_tier, flash_attn_forward
 
 _DTYPES = (torch.float16, torch.bfloat16, torch.float32)
 
-# Crossover of this engine over stock SDPA on B200 (calibrate(), bf16/fp16, D 64/128, causal
-# and not): below this length stock SDPA's launch-light fused kernels win or tie.
-DEFAULT_FAST_MIN_SEQ = 1024
+# Crossover of this engine over stock SDPA, measured by calibrate() on B200 with torch 2.11
+# (bf16, D 64/128, causal and not, L 256-8192, 16 heads): stock SDPA (its cuDNN attention on
+# this GPU) was faster on every shape, by 12-19% at L = 8192 and more at short lengths, so by
+# default no call is routed for speed. MTLFLASHATTN_SDPA_FAST_MIN_SEQ (or fast_min_seq) turns
+# the gate on where calibrate() finds a crossover (e.g. a torch build without that backend).
+DEFAULT_FAST_MIN_SEQ = None
 DEFAULT_MIN_GB = 12.0
 
 
@@ -107,7 +110,8 @@ def _decide(q, k, v, attn_mask, dropout_p, is_causal, enable_gqa=True):
     longest = max(Lq, Lk)
     if _g.min_seq is not None and longest >= _g.min_seq:
         return True, "correctness-large-seq"
-    if longest >= _g.fast_min_seq and _select_tier(q, k, v) == "tcgen05":
+    if (_g.fast_min_seq is not None and longest >= _g.fast_min_seq
+            and _select_tier(q, k, v) == "tcgen05"):
         return True, "fast-tier"
     scores = B * Hq * Lq * Lk * 2
     if scores >= _g.min_score_bytes:
