@@ -200,6 +200,23 @@ def _packed(*args):
     return buf
 
 
+_workspaces = {}  # (device, stream) -> uint8 tensor
+
+
+def _workspace(dev, stream, need):
+    """Split-KV scratch for launches on ``stream``: one buffer per (device, stream), grown on
+    demand and reused by every later call. Work on one stream runs in order, so a call never
+    overwrites partials an earlier call still reads; a replaced buffer goes back to torch's
+    caching allocator, which keeps it until the work queued on its stream is done. Saves a
+    torch.empty per decode-sized call."""
+    key = (dev, stream)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=dev)
+        _workspaces[key] = ws
+    return ws
+
+
 def _run(p, q, what, causal, trace_shape, kernel, D):
     dev = q.device
     ctx = torch.cuda.device(dev) if dev.index != torch.cuda.current_device() else None
@@ -210,13 +227,12 @@ def _run(p, q, what, causal, trace_shape, kernel, D):
             sel = _lib.select_kernel(p)
             label = "cuda/" + _lib.KERNEL_NAMES.get(sel, "rejected")
             _record_trace(q.dtype, trace_shape[0], trace_shape[1], trace_shape[2], causal, label)
-        ws = None
+        stream = torch.cuda.current_stream(dev).cuda_stream
         need = _lib.workspace_size(p)
         if need > 0:  # few query rows: let the library split the keys over more CTAs
-            ws = torch.empty(need, dtype=torch.uint8, device=dev)
+            ws = _workspace(dev, stream, need)
             _WS.pack_into(p, _lib.WORKSPACE_OFFSET, ws.data_ptr(), need)
-        rc = _lib.fwd(p, torch.cuda.current_stream(dev).cuda_stream)
-        del ws  # the caching allocator keeps it alive for work already queued on this stream
+        rc = _lib.fwd(p, stream)
         if rc != _lib.OK:
             if rc == _lib.ERR_UNSUPPORTED and kernel != _lib.KERNEL_AUTO:
                 raise RuntimeError(

@@ -122,15 +122,19 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 #ifndef MFA_EMU128
 #define MFA_EMU128 0
 #endif
-// The same for the softcap kernel (kBias = 2), whose three MUFU operations per score (two ex2
-// and a reciprocal, or an ex2 and a tanh) make it MUFU-bound.
+// The same for the softcap kernel (kBias = 2), which is MUFU-bound: two MUFU operations per
+// score (tanh and the softmax ex2). Measured on B200, config 3 (fp16 D = 128, softcap 30,
+// window 1024/1024), TFLOP/s: ex2+rcp tanh 365 (kEmu 0), 368 (2), 362 (4); hardware tanh
+// 424 (0), 442 (2), 429 (4).
 #ifndef MFA_EMU_SOFTCAP
-#define MFA_EMU_SOFTCAP 0
+#define MFA_EMU_SOFTCAP 2
 #endif
-// Softcap tanh: 0 = 1 - 2 / (2^(2 y log2e) + 1) with MUFU ex2 and rcp (or Newton); 1 = the
-// hardware tanh.approx (one MUFU operation instead of two).
+// Softcap tanh: 1 = the hardware tanh.approx.f32 (one MUFU operation; its error, ~2^-11
+// relative, moves a logit by at most cap * 2^-11, and config 3's output error against the fp32
+// oracle stayed at 1.4e-4); 0 = 1 - 2 / (2^(2 y log2e) + 1) with MUFU ex2 and a reciprocal
+// (MUFU or Newton, MFA_RCP_EMU), two MUFU operations.
 #ifndef MFA_SOFTCAP_TANH
-#define MFA_SOFTCAP_TANH 0
+#define MFA_SOFTCAP_TANH 1
 #endif
 // Score transform, a template parameter of the kernel:
 //   kBias = 0  x = s                        (c = scale*log2e folded into the exponent)
@@ -576,14 +580,16 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
             f2unpack(e2, ea, eb);
             uint64_t r2;
             if (((i >> 1) & 7) < MFA_RCP_EMU) {
-              // reciprocal on the FMA pipe: bit-trick guess (relative error < 1/8) and three
-              // Newton steps r += r(1 - d r) (error < 1e-7); d >= 1 is clamped below 2^126 so the
-              // guess stays a normal number (1/d < 1.2e-38 is 0 for the logit anyway)
+              // reciprocal on the FMA pipe: the guess bits(1/d) ~ kRcpSeed - bits(d) (relative
+              // error <= 0.051; the constant is fitted by csrc/fit_rcp_seed.py) and three Newton
+              // steps r += r(1 - d r) (error < 1e-7 after fp32 rounding); d >= 1 is clamped below
+              // 2^126 so the guess stays a normal number (1/d < 1.2e-38 is 0 for the logit anyway)
+              constexpr int kRcpSeed = 0x7EF311C2;
               ea = fminf(ea, 8.5e37f);
               eb = fminf(eb, 8.5e37f);
               const uint64_t nd = f2pack(-ea, -eb), one = f2pack(1.f, 1.f);
-              r2 = f2pack(__int_as_float(0x7EF311C3 - __float_as_int(ea)),
-                          __int_as_float(0x7EF311C3 - __float_as_int(eb)));
+              r2 = f2pack(__int_as_float(kRcpSeed - __float_as_int(ea)),
+                          __int_as_float(kRcpSeed - __float_as_int(eb)));
 #pragma unroll
               for (int it = 0; it < 3; ++it) r2 = ffma2(r2, ffma2(nd, r2, one), r2);
             } else {
