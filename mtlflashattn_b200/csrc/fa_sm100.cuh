@@ -126,6 +126,16 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 // score (tanh and the softmax ex2). Measured on B200, config 3 (fp16 D = 128, softcap 30,
 // window 1024/1024), TFLOP/s: ex2+rcp tanh 365 (kEmu 0), 368 (2), 362 (4); hardware tanh
 // 424 (0), 442 (2), 429 (4).
+// kHalfExp: of every 8 pairs of probabilities of the plain kernel (kBias = 0), how many are
+// computed by one packed 16-bit MUFU ex2 (ex2_x2: two results per operation, P in its final
+// 16-bit type with no conversion) instead of two fp32 ones. Halves the MUFU time of those
+// pairs; the argument is rounded to 16 bits first.
+#ifndef MFA_HALF_EXP64
+#define MFA_HALF_EXP64 0
+#endif
+#ifndef MFA_HALF_EXP128
+#define MFA_HALF_EXP128 0
+#endif
 #ifndef MFA_EMU_SOFTCAP
 #define MFA_EMU_SOFTCAP 2
 #endif
@@ -200,7 +210,8 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
 template <int DP, bool kBF16, int kBias, int CG = DefaultCG<kBias>::value,
           int TILES = DefaultTiles<DP, CG>::value, bool kPack = false,
           int kEmu = (kBias == 2 ? MFA_EMU_SOFTCAP
-                                 : DP == 64 ? (TILES == 1 ? MFA_EMU64 : 0) : MFA_EMU128)>
+                                 : DP == 64 ? (TILES == 1 ? MFA_EMU64 : 0) : MFA_EMU128),
+          int kHalfExp = (kBias == 0 ? (DP == 64 ? MFA_HALF_EXP64 : MFA_HALF_EXP128) : 0)>
 __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
                                   sm100::Roles<CG, TILES>::kCtasPerSm)
     fa_fwd_sm100(const __grid_constant__ Sm100Args args) {
@@ -683,6 +694,25 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
         for (int i = 0; i < 16; ++i) {
           const int e = 32 * cc + 2 * i;
           const uint64_t t2 = ffma2(f2pack(x[e], x[e + 1]), c2, nref2);
+          if ((i & 7) >= 8 - kHalfExp) {
+            // one MUFU operation for the pair; P is produced in its 16-bit type directly and
+            // the row sum adds exactly the values P.V will use
+            float ta, tb;
+            f2unpack(t2, ta, tb);
+            const uint32_t ph = ex2_x2<kBF16>(pack2<kBF16>(ta, tb));
+            pk[i] = ph;
+            float p0, p1;
+            if constexpr (kBF16) {
+              p0 = __uint_as_float(ph << 16);
+              p1 = __uint_as_float(ph & 0xFFFF0000u);
+            } else {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ph));
+              p0 = f.x;
+              p1 = f.y;
+            }
+            if (i & 1) acc1 = fadd2(acc1, f2pack(p0, p1)); else acc0 = fadd2(acc0, f2pack(p0, p1));
+            continue;
+          }
           uint64_t p2;
           if ((i & 7) < kEmu) {
             p2 = exp2_poly2(t2);

@@ -369,3 +369,20 @@ def test_api_errors_on_gpu():
         mp.setenv("MTLFLASHATTN_KERNEL", "tcgen05")
         with pytest.raises(RuntimeError):
             mfa.flash_attn_func(q.float(), k.float(), v.float())
+
+
+@pytest.mark.parametrize("kw", [dict(causal=True), dict(softcap=30.0), dict(softcap=5.0, causal=True),
+                                dict(alibi_slopes=torch.tensor([0.5, 0.25]))],
+                         ids=["large-logits", "softcap30", "softcap5-causal", "alibi-steep"])
+def test_fp32_path_accuracy_at_large_logits(kw):
+    """The fp32 CUDA-core kernel is built with fast-math intrinsics (__expf, __tanhf-style
+    approximations, approximate division). Measure its error where those matter most: logits
+    of magnitude ~50-100 (inputs scaled x4, D = 128), softcap saturation and steep ALiBi, against
+    the fp32 oracle. Bar: 5e-4 (the fp32 bar); the reference's fp32 TOL (2e-5 + 1e-4 rel) too."""
+    q, k, v = ref.make_qkv(1, 512, 700, 2, 2, 128, torch.float32, seed=11, scale_inputs=4.0)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    kwd = {a: (b.to(DEV) if torch.is_tensor(b) else b) for a, b in kw.items()}
+    out = mfa.flash_attn_func(qd, kd, vd, **kwd)
+    want = ref.flash_attn_func(q, k, v, **kw)
+    bar_check(out.cpu(), want, torch.float32, f"fp32 {list(kw)}")
+    check_close(out, want, torch.float32, f"fp32 {list(kw)}")
