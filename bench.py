@@ -8,10 +8,12 @@ The default workload is BASELINE config 5, the one the metric quotes at 1/2/4/8 
 the whole problem over inputs already resident in HBM (``value``). With N ranks the heads are
 sharded over the ranks (KV-group-aligned, no communication): strong scaling, ``value`` = the
 whole problem's FLOPs over the max-over-ranks device time. At N > 1 the same line carries a
-``split_kv`` leg: every rank holds the zigzag key chunks g and 2N-1-g of all heads, computes
-partials for every query row, and the partials are merged over NCCL (all-gather of the row
-log-sum-exp, one rescale kernel, reduce-scatter by query rows); its rate and the collectives'
-share of each step are timed with CUDA events. Every run checks sampled row windows of its
+``split_kv`` leg: every rank holds one contiguous key range of all heads with equal causal
+work and computes partials for every query row; the forward scatters each partial row into the
+receive buffer of the rank that owns it (peer stores over NVLink) and each rank merges its own
+rows locally. The same leg with the NCCL merge (all-gather of the row log-sum-exp, rescale
+kernel, reduce-scatter by query rows) is reported beside it. Phases are timed with CUDA
+events. Every run checks sampled row windows of its
 output against a single-GPU forward of the same rows (``parity``).
 
 ``e2e`` is the same workload through the public host-memory API (``flash_attn_host``): pinned
@@ -343,12 +345,14 @@ def measure(cfg, dev, steps, warmup, flush, stream, rank=0, world=1):
     return times, flops, nbytes, desc, call, dev_in, host_in, last[0]
 
 
-def split_kv_leg(steps, warmup, dev, rank, world, flush, stream, dist):
-    """Config 5 as split-KV over the ranks: rank g holds the zigzag key chunks g and 2N-1-g of
-    every head (all ranks draw the same seeded q/k/v on the device), computes partials for all
-    131072 query rows and the merge leaves each rank its own rows. Per step, CUDA events on the
-    launching stream time the forwards, the log-sum-exp all-gather, the rescale kernel and the
-    reduce-scatter; every figure is the max over ranks."""
+def split_kv_leg(steps, warmup, dev, rank, world, flush, stream, dist, merge):
+    """Config 5 as split-KV over the ranks: rank g holds one contiguous key range of all heads
+    with equal causal work (balanced_ranges; all ranks draw the same seeded q/k/v on the
+    device), computes partials for all 131072 query rows, and the merge leaves each rank its
+    own rows. merge = "peer": the forward scatters partial rows into their owners' receive
+    buffers over NVLink, then one local merge kernel; "nccl": all-gather of the row
+    log-sum-exp, rescale kernel, reduce-scatter. Per step, CUDA events on the launching stream
+    time the phases; every figure is the max over ranks."""
     from mtlflashattn_b200 import distributed as mfd
 
     B, L, H, D, dt, causal, _, sc = DENSE["5"]
@@ -356,13 +360,14 @@ def split_kv_leg(steps, warmup, dev, rank, world, flush, stream, dist):
     q = (torch.randn(B, L, H, D, device=dev, generator=gen) * sc).to(dt)
     k = (torch.randn(B, L, H, D, device=dev, generator=gen) * sc).to(dt)
     v = (torch.randn(B, L, H, D, device=dev, generator=gen) * sc).to(dt)
-    rng = mfd.zigzag_ranges(L, world, rank)
+    rng = mfd.balanced_ranges(L, world, rank, causal=True)
     kp = [k[:, a:b].contiguous() for a, b in rng]
     vp = [v[:, a:b].contiguous() for a, b in rng]
     last = []
 
     def one(ev=None):
-        last[:] = [mfd.flash_attn_split_kv(q, kp, vp, rng, L, causal=True, events=ev)]
+        last[:] = [mfd.flash_attn_split_kv(q, kp, vp, rng, L, causal=True, events=ev,
+                                           merge=merge)]
 
     for _ in range(warmup):
         one()
@@ -379,35 +384,41 @@ def split_kv_leg(steps, warmup, dev, rank, world, flush, stream, dist):
         e.record(stream)
         parts.append((s, e, ev))
     torch.cuda.synchronize()
-    tot = fwd = gat = resc = rs = 0.0
+    acc = {}
     for s, e, ev in parts:
-        tot += s.elapsed_time(e)
-        fwd += s.elapsed_time(ev["forward_done"])
-        gat += ev["lse_gather"][0].elapsed_time(ev["lse_gather"][1])
-        resc += ev["lse_gather"][1].elapsed_time(ev["reduce_scatter"][0])
-        rs += ev["reduce_scatter"][0].elapsed_time(ev["reduce_scatter"][1])
-    t = torch.tensor([tot, fwd, gat, resc, rs], device=dev, dtype=torch.float64) / steps
+        fwd = ev["forward_done"]
+        ph = {"total": s.elapsed_time(e), "forward": s.elapsed_time(fwd)}
+        if merge == "peer":
+            ph["exchange_wait"] = fwd.elapsed_time(ev["exchange_done"])
+            ph["local_merge"] = ev["exchange_done"].elapsed_time(e)
+        else:
+            ph["lse_allgather"] = ev["lse_gather"][0].elapsed_time(ev["lse_gather"][1])
+            ph["rescale"] = ev["lse_gather"][1].elapsed_time(ev["reduce_scatter"][0])
+            ph["reduce_scatter"] = ev["reduce_scatter"][0].elapsed_time(ev["reduce_scatter"][1])
+        for name, val in ph.items():
+            acc[name] = acc.get(name, 0.0) + val / steps
+    names = sorted(acc)
+    t = torch.tensor([acc[n] for n in names], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    tot, fwd, gat, resc, rs = t.tolist()
+    acc = dict(zip(names, t.tolist()))
     out, (r0, r1) = last[0]
     diff = window_diff(q, k, v, out, sample_windows(r0, r1), row0=r0)
     dd = torch.tensor([diff], device=dev, dtype=torch.float64)
     dist.all_reduce(dd, op=dist.ReduceOp.MAX)
     flops = attention_flops(B, H, L, L, D, causal)
-    return {
+    tot = acc["total"]
+    res = {
         "value": round(flops / (tot * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
-        "ms_per_step": round(tot, 4), "steps": steps,
-        "forward_ms": round(fwd, 4), "lse_allgather_ms": round(gat, 4),
-        "rescale_ms": round(resc, 4), "reduce_scatter_ms": round(rs, 4),
-        "collective_share": round((gat + rs) / tot, 4),
-        "merge_share": round((tot - fwd) / tot, 4),
-        "layout": "rank g: zigzag key chunks g and 2N-1-g of all 16 heads, all 131072 query "
-                  "rows; merge = all-gather of row log-sum-exp (fp32 [16, 131072]), one "
-                  "mfa_lse_rescale_sum kernel, NCCL reduce-scatter by query rows of fp32 "
-                  "[131072, 16, 128]; each rank ends with ceil(L/N) rows",
+        "ms_per_step": round(tot, 4), "steps": steps, "merge": merge,
+        "phases_ms": {n: round(acc[n], 4) for n in names if n != "total"},
+        "merge_share": round((tot - acc["forward"]) / tot, 4),
+        "key_ranges": "one contiguous range per rank with equal causal work",
         "parity": {"max_abs_diff_vs_single_gpu": round(dd.item(), 6), "ok": dd.item() <= 2e-2,
                    "windows_per_rank": len(sample_windows(r0, r1))},
     }
+    if merge == "nccl":
+        res["collective_share"] = round((acc["lse_allgather"] + acc["reduce_scatter"]) / tot, 4)
+    return res
 
 
 def run_gpu(args):
@@ -504,7 +515,10 @@ def run_gpu(args):
     if world > 1 and args.config == "5" and not args.no_split_kv:
         torch.cuda.empty_cache()
         split = split_kv_leg(min(args.steps, args.split_steps), args.warmup, dev, rank, world,
-                             flush, stream, dist)
+                             flush, stream, dist, "peer")
+        torch.cuda.empty_cache()
+        split["nccl_merge"] = split_kv_leg(min(args.steps, args.split_steps), args.warmup, dev,
+                                           rank, world, flush, stream, dist, "nccl")
         torch.cuda.empty_cache()
 
     configs = None

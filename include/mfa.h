@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define MFA_ABI_VERSION 5
+#define MFA_ABI_VERSION 6
 
 /* Status codes. The Python layer maps them to the reference's exception types. */
 enum mfa_status {
@@ -158,6 +158,47 @@ int mfa_lse_combine(const float* const* o_part, const float* const* lse_part, in
 int mfa_lse_rescale_sum(const float* const* o_part, const float* const* lse_part, int32_t n,
                         int32_t rows, int32_t H, int32_t D, const float* lse_ref, void* o,
                         int32_t o_dtype, void* cuda_stream);
+
+/* ---- split-KV over several GPUs, merged through peer memory (no counterpart in the
+ * reference, which runs on one Apple GPU). The query rows are owned by GPUs in contiguous
+ * blocks of rows_per_peer; every GPU holds some of the keys. mfa_fwd_scatter runs this GPU's
+ * forward over its keys and its epilogue stores each fp32 partial row (normalised by its own
+ * softmax sum) and the row log-sum-exp straight into the OWNING GPU's receive buffers, slot
+ * `slot`, with plain stores over NVLink, so the exchange overlaps the attention itself. After
+ * every GPU's scatter has completed (the caller orders that, e.g. with an NCCL all-reduce on a
+ * one-element tensor), each GPU merges the slots of its own rows locally with mfa_lse_merge.
+ * Receive buffers come from mfa_peer_alloc on their own GPU and are mapped on the others with
+ * mfa_peer_open (CUDA IPC handles of MFA_IPC_HANDLE_BYTES bytes, exchanged by the caller). */
+#define MFA_MAX_PEERS 8
+#define MFA_IPC_HANDLE_BYTES 64
+typedef struct mfa_peer_scatter {
+  int32_t n_peers;        /* GPUs owning query rows (1..MFA_MAX_PEERS) */
+  int32_t rows_per_peer;  /* GPU g owns rows [g * rows_per_peer, (g + 1) * rows_per_peer) */
+  int32_t slot;           /* slot of this launch in every receive buffer (e.g. its rank) */
+  float* o_recv[MFA_MAX_PEERS];   /* GPU g's receive buffer, mapped here: fp32
+                                     [slots][rows_per_peer][B][Hq][D], 16-byte aligned */
+  float* lse_recv[MFA_MAX_PEERS]; /* fp32 [slots][B * Hq][rows_per_peer] */
+} mfa_peer_scatter;
+
+/* mfa_fwd with its output scattered by query row to the owning GPUs (see above). Dense inputs,
+ * the tcgen05 kernel (fp16/bf16, D % 8 == 0); p->o and p->lse are ignored, p->Lq must be
+ * <= n_peers * rows_per_peer, and the caller guarantees every slot index < the buffers' slot
+ * count. p->k_pos_offset / p->lk_total place this GPU's keys in the whole sequence. */
+int mfa_fwd_scatter(const mfa_fwd_params* p, const mfa_peer_scatter* s, void* cuda_stream);
+
+/* Local log-sum-exp merge of n partials of the same rows: o_parts fp32 [n][rows][H][D],
+ * lse_parts fp32 [n][H][rows] (a receive buffer as mfa_fwd_scatter fills it, H = B * Hq).
+ * Writes o [rows][H][D] in o_dtype and, if lse != NULL, lse [H][rows]. */
+int mfa_lse_merge(const float* o_parts, const float* lse_parts, int32_t n, int32_t rows,
+                  int32_t H, int32_t D, void* o, int32_t o_dtype, float* lse, void* cuda_stream);
+
+/* Receive buffers for mfa_fwd_scatter: device memory on the current GPU plus its CUDA IPC
+ * handle (MFA_IPC_HANDLE_BYTES bytes written to ipc_handle). */
+int mfa_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+/* Map another GPU's receive buffer (from its IPC handle) into this process. */
+int mfa_peer_open(const void* ipc_handle, void** ptr);
+int mfa_peer_close(void* ptr);   /* unmap a buffer mapped by mfa_peer_open */
+int mfa_peer_free(void* ptr);    /* free a buffer from mfa_peer_alloc */
 
 /* Host buffers of mfa_fwd_staged. */
 typedef struct {

@@ -13,7 +13,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmfa.so")
 
-MFA_ABI_VERSION = 5
+MFA_ABI_VERSION = 6
 
 # mfa_status
 OK = 0
@@ -43,6 +43,12 @@ EXPORTED_SYMBOLS = (
     "mfa_select_kernel",
     "mfa_lse_combine",
     "mfa_lse_rescale_sum",
+    "mfa_fwd_scatter",
+    "mfa_lse_merge",
+    "mfa_peer_alloc",
+    "mfa_peer_open",
+    "mfa_peer_close",
+    "mfa_peer_free",
     "mfa_selftest_wait_timeout",
     "mfa_status_string",
     "mfa_abi_version",
@@ -96,6 +102,22 @@ class MfaFwdParams(ctypes.Structure):
 # let a caller patch them after sizing the workspace.
 PARAMS_FORMAT = "<5Q12q2q6i2Q2i2f3i4xQ5i4xQQQ"
 WORKSPACE_OFFSET = 264  # workspace pointer, then workspace_bytes
+
+
+MAX_PEERS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class MfaPeerScatter(ctypes.Structure):
+    """Mirror of ``struct mfa_peer_scatter`` (include/mfa.h)."""
+
+    _fields_ = [
+        ("n_peers", ctypes.c_int32),
+        ("rows_per_peer", ctypes.c_int32),
+        ("slot", ctypes.c_int32),
+        ("o_recv", ctypes.c_void_p * MAX_PEERS),
+        ("lse_recv", ctypes.c_void_p * MAX_PEERS),
+    ]
 
 
 class MfaHostIo(ctypes.Structure):
@@ -166,6 +188,23 @@ def load(path: str | None = None) -> ctypes.CDLL:
             ctypes.c_int32, ctypes.c_void_p,
         ]
         lib.mfa_lse_rescale_sum.restype = ctypes.c_int
+        lib.mfa_fwd_scatter.argtypes = [ctypes.c_void_p, ctypes.POINTER(MfaPeerScatter),
+                                        ctypes.c_void_p]
+        lib.mfa_fwd_scatter.restype = ctypes.c_int
+        lib.mfa_lse_merge.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                      ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                      ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
+                                      ctypes.c_void_p]
+        lib.mfa_lse_merge.restype = ctypes.c_int
+        lib.mfa_peer_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p),
+                                       ctypes.c_void_p]
+        lib.mfa_peer_alloc.restype = ctypes.c_int
+        lib.mfa_peer_open.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+        lib.mfa_peer_open.restype = ctypes.c_int
+        lib.mfa_peer_close.argtypes = [ctypes.c_void_p]
+        lib.mfa_peer_close.restype = ctypes.c_int
+        lib.mfa_peer_free.argtypes = [ctypes.c_void_p]
+        lib.mfa_peer_free.restype = ctypes.c_int
         lib.mfa_selftest_wait_timeout.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]
         lib.mfa_selftest_wait_timeout.restype = ctypes.c_int
         lib.mfa_status_string.argtypes = [ctypes.c_int]
@@ -234,3 +273,38 @@ def lse_rescale_sum(o_ptrs, lse_ptrs, rows, H, D, lse_ref_ptr, o_ptr, o_dtype, s
     la = (ctypes.c_void_p * n)(*lse_ptrs)
     return load().mfa_lse_rescale_sum(oa, la, n, rows, H, D, ctypes.c_void_p(lse_ref_ptr),
                                       ctypes.c_void_p(o_ptr), o_dtype, ctypes.c_void_p(stream))
+
+
+def fwd_scatter(params, scatter: MfaPeerScatter, stream: int) -> int:
+    return load().mfa_fwd_scatter(_addr(params), ctypes.byref(scatter), stream)
+
+
+def lse_merge(o_parts_ptr, lse_parts_ptr, n, rows, H, D, o_ptr, o_dtype, lse_ptr, stream) -> int:
+    return load().mfa_lse_merge(o_parts_ptr, lse_parts_ptr, n, rows, H, D, o_ptr, o_dtype,
+                                lse_ptr or None, stream)
+
+
+def peer_alloc(nbytes: int):
+    """(device pointer, IPC handle bytes) of a new receive buffer on the current GPU."""
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    rc = load().mfa_peer_alloc(nbytes, ctypes.byref(ptr), handle)
+    if rc != OK:
+        raise MfaError(rc, "mfa_peer_alloc")
+    return ptr.value, handle.raw
+
+
+def peer_open(handle: bytes) -> int:
+    ptr = ctypes.c_void_p()
+    rc = load().mfa_peer_open(ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES), ctypes.byref(ptr))
+    if rc != OK:
+        raise MfaError(rc, "mfa_peer_open")
+    return ptr.value
+
+
+def peer_close(ptr: int) -> int:
+    return load().mfa_peer_close(ptr)
+
+
+def peer_free(ptr: int) -> int:
+    return load().mfa_peer_free(ptr)

@@ -8,6 +8,8 @@
 namespace mfa {
 
 // Resolved arguments as both kernels read them. Strides are in elements.
+constexpr int kMaxPeers = 8;  // GPUs one split-KV launch can scatter its partial rows to
+
 struct FwdArgs {
   const void* q;
   const void* k;
@@ -51,6 +53,15 @@ struct FwdArgs {
   int pack_shift;
   // sequences of a varlen launch (B before the split merge views the packed rows as one batch)
   int nseq;
+  // split-KV over several GPUs (peer_n > 0; dense launches only): query row R is owned by GPU
+  // R / peer_rows, and this launch's fp32 partial row and row log-sum-exp go straight into that
+  // GPU's receive buffers (peer-mapped device pointers), in slot peer_slot of each:
+  // peer_o[g] + peer_slot * peer_slot_o holds [peer_rows][B][Hq][D] (o_* strides below), and
+  // peer_lse[g] + peer_slot * peer_slot_lse holds [B*Hq][peer_rows] (lse_* strides)
+  int peer_n, peer_rows, peer_slot;
+  int64_t peer_slot_o, peer_slot_lse;
+  float* peer_o[kMaxPeers];
+  float* peer_lse[kMaxPeers];
 };
 
 // One (batch, sequence) view after resolving dense vs varlen.
@@ -133,6 +144,13 @@ __device__ __forceinline__ void store_row_chunk(const FwdArgs& a, void* row_ptr,
                                                 const float* vals, int n) {
   if (a.o_dtype == 2) {
     float* p = reinterpret_cast<float*>(row_ptr) + col0;
+    if (a.o_vec16 && n == 32) {  // 16-byte stores (also the unit of a remote write over NVLink)
+      float4* dst = reinterpret_cast<float4*>(p);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        dst[i] = make_float4(vals[4 * i], vals[4 * i + 1], vals[4 * i + 2], vals[4 * i + 3]);
+      return;
+    }
 #pragma unroll
     for (int i = 0; i < 32; ++i)
       if (i < n) p[i] = vals[i];

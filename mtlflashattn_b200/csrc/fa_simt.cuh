@@ -254,6 +254,74 @@ __global__ void lse_rescale_sum_kernel(const __grid_constant__ PartPtrs pp, int 
   }
 }
 
+// Local merge of n partials of the same rows held in one buffer (the receive buffer of a
+// split-KV over GPUs): parts fp32 [n][rows][H][D] (partial g at parts + g * part_stride), each
+// normalised by its own softmax sum, lses fp32 [n][H][rows] (lses + g * lse_stride). Writes
+// o [rows][H][D] in TO and optionally lse_out [H][rows]: lse = log sum_g exp(lse_g),
+// o = sum_g exp(lse_g - lse) o_g; rows no partial attends get 0 and -inf. One warp per
+// (row, head); lanes own four consecutive columns when vec4.
+template <typename TO>
+__global__ void lse_merge_kernel(const float* __restrict__ parts, const float* __restrict__ lses,
+                                 int n, int rows, int H, int D, int64_t part_stride,
+                                 int64_t lse_stride, TO* o, float* lse_out, int vec4) {
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (int64_t)rows * H) return;
+  const int row = (int)(w / H), h = (int)(w % H);
+  const int64_t li = (int64_t)h * rows + row;
+  const int64_t oi = ((int64_t)row * H + h) * D;
+  float mx = -INFINITY;
+  for (int g = 0; g < n; ++g) mx = fmaxf(mx, lses[g * lse_stride + li]);
+  float tot = 0.f;
+  if (mx != -INFINITY)
+    for (int g = 0; g < n; ++g) {
+      const float lg = lses[g * lse_stride + li];
+      if (lg != -INFINITY) tot += expf(lg - mx);
+    }
+  const float lse = mx == -INFINITY ? -INFINITY : mx + logf(tot);
+  const float inv = mx == -INFINITY ? 0.f : 1.f / tot;
+  auto put = [&](int d, float v) {
+    if constexpr (sizeof(TO) == 4) {
+      o[oi + d] = v;
+    } else {
+      o[oi + d] = TO(v);
+    }
+  };
+  if (vec4) {
+    for (int c = 4 * lane; c < D; c += 128) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int g = 0; g < n && mx != -INFINITY; ++g) {
+        const float lg = lses[g * lse_stride + li];
+        if (lg == -INFINITY) continue;  // a partial that saw no key of this row
+        const float wg = expf(lg - mx) * inv;
+        const float4 x = *reinterpret_cast<const float4*>(parts + g * part_stride + oi + c);
+        acc.x = fmaf(wg, x.x, acc.x);
+        acc.y = fmaf(wg, x.y, acc.y);
+        acc.z = fmaf(wg, x.z, acc.z);
+        acc.w = fmaf(wg, x.w, acc.w);
+      }
+      if constexpr (sizeof(TO) == 4) {
+        *reinterpret_cast<float4*>(o + oi + c) = acc;
+      } else {
+        put(c, acc.x);
+        put(c + 1, acc.y);
+        put(c + 2, acc.z);
+        put(c + 3, acc.w);
+      }
+    }
+  } else {
+    for (int d = lane; d < D; d += 32) {
+      float acc = 0.f;
+      for (int g = 0; g < n && mx != -INFINITY; ++g) {
+        const float lg = lses[g * lse_stride + li];
+        if (lg != -INFINITY) acc = fmaf(expf(lg - mx) * inv, parts[g * part_stride + oi + d], acc);
+      }
+      put(d, acc);
+    }
+  }
+  if (lane == 0 && lse_out != nullptr) lse_out[li] = lse;
+}
+
 // Merge of the key splits of one launch (dense layout): partial outputs ws_o fp32
 // [split][B][Lq][Hq][D] normalised by their own sums, row log-sum-exp ws_lse [split][B][Hq][Lq].
 // One block of kCombineThreads per (batch, head, row). The split weights exp(lse_s - max) are

@@ -767,11 +767,20 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
       }
       const float inv = l > 0.f ? 1.f / l : 0.f;
       uint8_t* orow = nullptr;
+      // output row: this GPU's buffer, or (split-KV over GPUs) the owning GPU's receive slot
+      int64_t orow_idx = sv.q0 + row;
+      float* lse_base = a.lse;
+      uint8_t* obase = reinterpret_cast<uint8_t*>(a.o);
+      if (a.peer_n > 0 && store) {  // the host checked Lq <= peer_n * peer_rows
+        const int owner = (int)(orow_idx / a.peer_rows);
+        orow_idx -= (int64_t)owner * a.peer_rows;
+        obase = reinterpret_cast<uint8_t*>(a.peer_o[owner] + a.peer_slot * a.peer_slot_o);
+        lse_base = a.peer_lse[owner] + a.peer_slot * a.peer_slot_lse;
+      }
       if (store) {
         const int64_t esz = a.o_dtype == 2 ? 4 : 2;
-        orow = reinterpret_cast<uint8_t*>(a.o) +
-               esz * ((int64_t)split * a.o_split_stride + (int64_t)sv.qb * a.o_sb +
-                      (int64_t)(sv.q0 + row) * a.o_ss + (int64_t)h * a.o_sh);
+        orow = obase + esz * ((int64_t)split * a.o_split_stride + (int64_t)sv.qb * a.o_sb +
+                              orow_idx * a.o_ss + (int64_t)h * a.o_sh);
       }
 #pragma unroll 1
       for (int cc = cg * (DP / CG); cc < (cg + 1) * (DP / CG); cc += 32) {
@@ -789,10 +798,10 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
         const int nc = min(32, a.D - cc);
         if (store && nc > 0) store_row_chunk(a, orow, cc, vals, nc);
       }
-      if (store && cg == 0 && a.lse != nullptr) {
+      if (store && cg == 0 && lse_base != nullptr) {
         const float lse = l > 0.f ? (m_used * c + __log2f(l)) * 0.6931471805599453f : -INFINITY;
-        a.lse[(int64_t)split * a.lse_split_stride + (int64_t)sv.qb * a.lse_sb +
-              (int64_t)h * a.lse_sh + sv.q0 + row] = lse;
+        lse_base[(int64_t)split * a.lse_split_stride + (int64_t)sv.qb * a.lse_sb +
+                 (int64_t)h * a.lse_sh + orow_idx] = lse;
       }
     }
   }

@@ -16,6 +16,8 @@
 #include "fa_simt.cuh"
 #include "fa_sm100.cuh"
 
+static_assert(mfa::kMaxPeers == MFA_MAX_PEERS, "peer table size differs from the header's");
+
 namespace mfa {
 namespace {
 
@@ -741,6 +743,110 @@ int mfa_lse_rescale_sum(const float* const* o_part, const float* const* lse_part
   else
     mfa::lse_rescale_sum_kernel<__half><<<nb, 256, 0, st>>>(pp, n, rows, H, D, lse_ref, (__half*)o, v4);
   return cudaGetLastError() == cudaSuccess ? MFA_OK : MFA_ERR_CUDA;
+}
+
+int mfa_fwd_scatter(const mfa_fwd_params* p, const mfa_peer_scatter* sc, void* stream) {
+  if (mfa::fault_injected("fwd")) return MFA_ERR_FAULT_INJECTED;
+  if (sc == nullptr) return MFA_ERR_INVALID;
+  int rc = mfa::validate(p);
+  if (rc != MFA_OK) return rc;
+  if (p->cu_q != nullptr) return MFA_ERR_UNSUPPORTED;  // dense launches only
+  if (sc->n_peers < 1 || sc->n_peers > mfa::kMaxPeers || sc->rows_per_peer < 1 || sc->slot < 0)
+    return MFA_ERR_INVALID;
+  if ((int64_t)p->Lq > (int64_t)sc->n_peers * sc->rows_per_peer) return MFA_ERR_INVALID;
+  for (int g = 0; g < sc->n_peers; ++g) {
+    if (sc->o_recv[g] == nullptr || sc->lse_recv[g] == nullptr) return MFA_ERR_INVALID;
+    if (!mfa::aligned16(sc->o_recv[g])) return MFA_ERR_INVALID;
+  }
+  if (p->B == 0 || p->Lq == 0) return MFA_OK;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MFA_ERR_NO_DEVICE;
+  if (mfa::pick_kernel(p, dev) != MFA_KERNEL_TCGEN05) return MFA_ERR_UNSUPPORTED;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  (void)cudaGetLastError();
+  mfa::FwdArgs a = mfa::resolve(p);
+  const int64_t rows = sc->rows_per_peer;
+  a.o = sc->o_recv[0];
+  a.o_dtype = MFA_FP32;
+  a.o_sb = (int64_t)p->Hq * p->D;
+  a.o_ss = (int64_t)p->B * p->Hq * p->D;
+  a.o_sh = p->D;
+  a.o_vec16 = 1;  // D % 8 == 0 (tcgen05) and 256-byte aligned receive buffers
+  a.lse = sc->lse_recv[0];
+  a.lse_sb = (int64_t)p->Hq * rows;
+  a.lse_sh = rows;
+  a.peer_n = sc->n_peers;
+  a.peer_rows = sc->rows_per_peer;
+  a.peer_slot = sc->slot;
+  a.peer_slot_o = rows * p->B * p->Hq * p->D;
+  a.peer_slot_lse = rows * p->B * p->Hq;
+  for (int g = 0; g < sc->n_peers; ++g) {
+    a.peer_o[g] = sc->o_recv[g];
+    a.peer_lse[g] = sc->lse_recv[g];
+  }
+  rc = mfa::run_sm100(p, a, dev, st, mfa::SplitPlan{}, nullptr);
+  if (rc != MFA_OK) return rc;
+  return cudaGetLastError() == cudaSuccess ? MFA_OK : MFA_ERR_CUDA;
+}
+
+int mfa_lse_merge(const float* o_parts, const float* lse_parts, int32_t n, int32_t rows,
+                  int32_t H, int32_t D, void* o, int32_t o_dtype, float* lse, void* stream) {
+  if (mfa::fault_injected("combine")) return MFA_ERR_FAULT_INJECTED;
+  if (n < 1 || rows < 0 || H < 1 || D < 1 || o_dtype < 0 || o_dtype > 2) return MFA_ERR_INVALID;
+  if (rows == 0) return MFA_OK;
+  if (o_parts == nullptr || lse_parts == nullptr || o == nullptr) return MFA_ERR_INVALID;
+  const int64_t part_stride = (int64_t)rows * H * D, lse_stride = (int64_t)rows * H;
+  const int v4 = (D % 4 == 0 && mfa::aligned16(o_parts) && mfa::aligned16(o)) ? 1 : 0;
+  const int64_t blocks = ((int64_t)rows * H * 32 + 255) / 256;
+  if (blocks >= (1ll << 31)) return MFA_ERR_UNSUPPORTED;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  (void)cudaGetLastError();
+  const unsigned nb = (unsigned)blocks;
+  if (o_dtype == MFA_FP32)
+    mfa::lse_merge_kernel<float><<<nb, 256, 0, st>>>(o_parts, lse_parts, n, rows, H, D,
+                                                      part_stride, lse_stride, (float*)o, lse, v4);
+  else if (o_dtype == MFA_BF16)
+    mfa::lse_merge_kernel<__nv_bfloat16><<<nb, 256, 0, st>>>(
+        o_parts, lse_parts, n, rows, H, D, part_stride, lse_stride, (__nv_bfloat16*)o, lse, v4);
+  else
+    mfa::lse_merge_kernel<__half><<<nb, 256, 0, st>>>(o_parts, lse_parts, n, rows, H, D,
+                                                       part_stride, lse_stride, (__half*)o, lse, v4);
+  return cudaGetLastError() == cudaSuccess ? MFA_OK : MFA_ERR_CUDA;
+}
+
+int mfa_peer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  if (ptr == nullptr || ipc_handle == nullptr || bytes == 0) return MFA_ERR_INVALID;
+  *ptr = nullptr;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return MFA_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return MFA_ERR_CUDA;
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return MFA_OK;
+}
+
+int mfa_peer_open(const void* ipc_handle, void** ptr) {
+  if (ptr == nullptr || ipc_handle == nullptr) return MFA_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  *ptr = nullptr;
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess
+             ? MFA_OK
+             : MFA_ERR_CUDA;
+}
+
+int mfa_peer_close(void* ptr) {
+  if (ptr == nullptr) return MFA_ERR_INVALID;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? MFA_OK : MFA_ERR_CUDA;
+}
+
+int mfa_peer_free(void* ptr) {
+  if (ptr == nullptr) return MFA_ERR_INVALID;
+  return cudaFree(ptr) == cudaSuccess ? MFA_OK : MFA_ERR_CUDA;
 }
 
 }  // extern "C"

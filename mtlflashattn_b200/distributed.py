@@ -21,9 +21,19 @@ Two decompositions, neither present in the reference (its tiers run on one Apple
      receives ``(W-1)/W`` of one fp32 output instead of all-reducing a whole one, and nobody
      holds rows it does not own unless it asks (``gather=True``).
 
-  The rank's two zigzag chunks are two launches of the forward kernel writing their partials
-  straight into the row-major layout (output strides), so no transpose or eager merge runs over
-  the partials.
+  The rank's key chunks are launches of the forward kernel writing their partials straight
+  into the row-major layout (output strides), so no transpose or eager merge runs over them.
+
+* Split-KV merged through peer memory (``merge="peer"``, the default on CUDA). The forward
+  kernel's epilogue stores every partial row directly into the receive buffer of the GPU that
+  owns the row (``mfa_fwd_scatter``: plain stores over NVLink into buffers mapped with CUDA
+  IPC), so the exchange runs while the attention runs, tile by tile; each GPU then merges its
+  own rows with one local kernel (``mfa_lse_merge``) that writes the final rows in the output
+  dtype. No all-gather, rescale pass or reduce-scatter remains. Ordering between GPUs comes
+  from two one-element NCCL all-reduces per call (receive buffers free before the scatter, all
+  partial rows landed before the merge); no kernel ever waits on another GPU. With
+  ``balanced_ranges`` each rank holds ONE contiguous key range of equal causal work, so a
+  rank makes one launch and each row has one partial per rank.
 
 The collectives are plain torch.distributed calls and run on any backend; the rescale is the
 library's CUDA kernel. Tests of the host logic on CPU (gloo) inject a CPU rescale instead.
@@ -56,6 +66,30 @@ def zigzag_ranges(L, world, rank):
         if bounds[c + 1] > bounds[c]:
             out.append((bounds[c], bounds[c + 1]))
     return out
+
+
+def balanced_ranges(Lk, world, rank, causal=True, Lq=None):
+    """One contiguous key range [k0, k1) for ``rank`` such that every rank's keys are attended
+    by the same number of (query, key) pairs. Non-causal: equal key counts. Causal with
+    bottom-right alignment: key j is seen by Lq - max(0, j - (Lk - Lq)) rows, so the early keys
+    weigh more and rank 0's range is the shortest (for Lq = Lk, boundary r sits near
+    Lk * (1 - sqrt(1 - r / world)))."""
+    Lq = Lk if Lq is None else Lq
+    if not causal:
+        return [((Lk * rank) // world, (Lk * (rank + 1)) // world)]
+    j = torch.arange(Lk, dtype=torch.float64)
+    seen = (Lq - (j - (Lk - Lq)).clamp_min(0)).clamp_min(0)
+    cum = torch.cumsum(seen, 0)
+    total = float(cum[-1]) if Lk > 0 else 0.0
+
+    def bound(r):
+        if r <= 0:
+            return 0
+        if r >= world:
+            return Lk
+        return int(torch.searchsorted(cum, total * r / world).item())
+
+    return [(bound(rank), bound(rank + 1))]
 
 
 def row_shard(Lq, world, rank):
@@ -155,21 +189,118 @@ def merge_partials(o_parts, lse_parts, group=None, rescale=None, events=None):
     return mine[: r1 - r0], lse_tot[:, r0:r1], (r0, r1)
 
 
+class _PeerBuffers:
+    """Receive buffers of one split-KV shape on every rank of a group, mapped on all of them.
+    One device allocation per rank (fp32 partial rows [slots][rows_per][BH][D] followed by the
+    row log-sum-exp [slots][BH][rows_per]), allocated by libmfa (cudaMalloc, so it can carry a
+    CUDA IPC handle), its handle all-gathered once and opened by every other rank."""
+
+    _cache = {}
+
+    def __init__(self, group, slots, rows_per, BH, D, device):
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        self.o_bytes = slots * rows_per * BH * D * 4
+        self.o_bytes += (-self.o_bytes) % 256
+        nbytes = self.o_bytes + slots * BH * rows_per * 4
+        with torch.cuda.device(device):
+            ptr, handle = _lib.peer_alloc(nbytes)
+            handles = [None] * world
+            dist.all_gather_object(handles, handle, group=group)
+            self.base = [ptr if g == rank else _lib.peer_open(handles[g]) for g in range(world)]
+        self.rank, self.world, self.device = rank, world, device
+        self.sync = torch.zeros(1, device=device)
+
+    @classmethod
+    def get(cls, group, slots, rows_per, BH, D, device):
+        key = (id(group), dist.get_world_size(group), slots, rows_per, BH, D, str(device))
+        buf = cls._cache.get(key)
+        if buf is None:
+            buf = cls._cache[key] = cls(group, slots, rows_per, BH, D, device)
+        return buf
+
+    def scatter_table(self, rows_per, slot):
+        sc = _lib.MfaPeerScatter()
+        sc.n_peers, sc.rows_per_peer, sc.slot = self.world, rows_per, slot
+        for g in range(self.world):
+            sc.o_recv[g] = self.base[g]
+            sc.lse_recv[g] = self.base[g] + self.o_bytes
+        return sc
+
+
+def _order(buf, group):
+    """Every rank's GPU work queued so far precedes what any rank queues next (a one-element
+    NCCL all-reduce on the current stream)."""
+    dist.all_reduce(buf.sync, group=group)
+
+
+def _split_kv_peer(q, k_parts, v_parts, key_ranges, lk_total, scale, causal, bias, group,
+                   out_dtype, events):
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    B, Lq, Hq, D = q.shape
+    nch = len(k_parts)
+    rows_per = -(-Lq // world)
+    buf = _PeerBuffers.get(group, world * nch, rows_per, B * Hq, D, q.device)
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    _order(buf, group)  # the previous call's merges have read their receive buffers
+    kernel = _kernel._tier_mode(q.dtype)
+    for c, (kp, vp, (a, _)) in enumerate(zip(k_parts, v_parts, key_ranges)):
+        kp, vp = _kernel._last_dim_contig(kp), _kernel._last_dim_contig(vp)
+        p = _kernel._packed(q, kp, vp, q, B, Hq, kp.shape[2], Lq, kp.shape[1], D, q.stride()[:3],
+                            kp.stride()[:3], vp.stride()[:3], q.stride()[:3], scale, causal, bias,
+                            kernel, None, (0, 0), None, None, 0, 0, a, lk_total)
+        rc = _lib.fwd_scatter(p, buf.scatter_table(rows_per, rank * nch + c), stream)
+        if rc != _lib.OK:
+            _kernel._raise_status(rc, "mfa_fwd_scatter")
+    if events is not None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        events["forward_done"] = ev
+    _order(buf, group)  # every rank's partial rows have landed in the owners' buffers
+    if events is not None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        events["exchange_done"] = ev
+    out = torch.empty(rows_per, B, Hq, D, device=q.device, dtype=out_dtype)
+    rc = _lib.lse_merge(buf.base[rank], buf.base[rank] + buf.o_bytes, world * nch, rows_per,
+                        B * Hq, D, out.data_ptr(), _kernel._DTYPES[out_dtype], None, stream)
+    if rc != _lib.OK:
+        _kernel._raise_status(rc, "mfa_lse_merge")
+    r0, r1 = row_shard(Lq, world, rank)
+    return out[: r1 - r0].transpose(0, 1), (r0, r1)
+
+
 def flash_attn_split_kv(q, k_parts, v_parts, key_ranges, lk_total, softmax_scale=None,
                         causal=False, window_size=(-1, -1), softcap=0.0, alibi_slopes=None,
-                        group=None, out_dtype=None, gather=False, events=None):
+                        group=None, out_dtype=None, gather=False, events=None, merge="auto"):
     """Attention of the full query set against keys spread over ranks.
 
     q: [B, Lq, Hq, D] (every rank); k_parts/v_parts: this rank's key chunks, each
     [B, n_i, Hkv, D], holding global key positions key_ranges[i] = (start, end) of lk_total.
     Returns (o_rows [B, r1 - r0, Hq, D] in out_dtype (default q.dtype), (r0, r1)): this rank's
     query rows of the merged output. With ``gather=True`` the rows of every rank are
-    all-gathered and the full [B, Lq, Hq, D] output is returned on every rank instead."""
+    all-gathered and the full [B, Lq, Hq, D] output is returned on every rank instead.
+
+    ``merge``: "peer" (partial rows scattered to their owners through peer memory by the
+    forward itself, then merged locally), "nccl" (all-gather of the row log-sum-exp, rescale,
+    reduce-scatter), or "auto": "peer" when the tensor-core kernel takes the inputs and the
+    group has at most 8 ranks, else "nccl". With "peer" every rank must pass the same number of
+    key chunks (each chunk has its slot in the receive buffers)."""
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q.shape[-1])
     B, Lq, Hq, D = q.shape
     alibi = (_kernel._broadcast_alibi_slopes(alibi_slopes, B, Hq, q.device)
              if alibi_slopes is not None else None)
     bias = _kernel._BiasParams(softcap, window_size[0], window_size[1], alibi)
+    world = dist.get_world_size(group)
+    if merge == "auto":
+        peer_ok = (q.is_cuda and world <= _lib.MAX_PEERS and q.shape[-1] % 8 == 0
+                   and q.dtype in (torch.float16, torch.bfloat16))
+        merge = "peer" if peer_ok else "nccl"
+    if merge == "peer":
+        out, rows = _split_kv_peer(q, k_parts, v_parts, key_ranges, lk_total, scale, causal,
+                                   bias, group, out_dtype or q.dtype, events)
+        return _gather_rows(out, rows, Lq, group) if gather else (out, rows)
     o_parts, lse_parts = [], []
     for kp, vp, (a, _) in zip(k_parts, v_parts, key_ranges):
         # partial rows straight into the row-major [Lq, B*Hq, D] layout the merge scatters
@@ -185,12 +316,17 @@ def flash_attn_split_kv(q, k_parts, v_parts, key_ranges, lk_total, softmax_scale
         events["forward_done"] = ev
     rows, _, (r0, r1) = merge_partials(o_parts, lse_parts, group=group, events=events)
     out = rows.view(r1 - r0, B, Hq, D).transpose(0, 1).to(out_dtype or q.dtype)
-    if not gather:
-        return out, (r0, r1)
+    return _gather_rows(out, (r0, r1), Lq, group) if gather else (out, (r0, r1))
+
+
+def _gather_rows(out, rows, Lq, group):
+    """All ranks' row blocks [B, r1 - r0, H, D] -> the full [B, Lq, H, D] on every rank."""
+    r0, r1 = rows
     world = dist.get_world_size(group)
     per = -(-Lq // world)
-    full = torch.zeros(world * per, B, Hq, D, device=q.device, dtype=out.dtype)
-    mine = torch.zeros(per, B, Hq, D, device=q.device, dtype=out.dtype)
+    B, _, H, D = out.shape
+    full = torch.zeros(world * per, B, H, D, device=out.device, dtype=out.dtype)
+    mine = torch.zeros(per, B, H, D, device=out.device, dtype=out.dtype)
     mine[: r1 - r0] = out.transpose(0, 1)
     dist.all_gather_into_tensor(full, mine, group=group)
     return full[:Lq].transpose(0, 1).contiguous()

@@ -37,11 +37,14 @@ def test_abi_version_and_status_strings():
 
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
-def test_ctypes_struct_matches_c_layout(tmp_path):
-    fields = [f[0] for f in _lib.MfaFwdParams._fields_]
+@pytest.mark.parametrize("cls,cname", [(_lib.MfaFwdParams, "mfa_fwd_params"),
+                                       (_lib.MfaPeerScatter, "mfa_peer_scatter"),
+                                       (_lib.MfaHostIo, "mfa_host_io")])
+def test_ctypes_struct_matches_c_layout(tmp_path, cls, cname):
+    fields = [f[0] for f in cls._fields_]
     src = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void){",
-           'printf("%zu\\n", sizeof(mfa_fwd_params));']
-    src += [f'printf("%zu\\n", offsetof(mfa_fwd_params, {f}));' for f in fields]
+           f'printf("%zu\\n", sizeof({cname}));']
+    src += [f'printf("%zu\\n", offsetof({cname}, {f}));' for f in fields]
     src += ["return 0;}"]
     c = tmp_path / "layout.c"
     c.write_text("\n".join(src))
@@ -49,9 +52,16 @@ def test_ctypes_struct_matches_c_layout(tmp_path):
     subprocess.run(["gcc", str(c), "-o", str(exe)], check=True)
     got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True,
                                           check=True).stdout.split()]
-    assert got[0] == ctypes.sizeof(_lib.MfaFwdParams)
+    assert got[0] == ctypes.sizeof(cls)
     for name, off in zip(fields, got[1:]):
-        assert getattr(_lib.MfaFwdParams, name).offset == off, name
+        assert getattr(cls, name).offset == off, name
+
+
+def test_packed_params_format_matches_struct():
+    """The hot path's struct.pack format has the C struct's size and workspace offset."""
+    import struct
+    assert struct.calcsize(_lib.PARAMS_FORMAT) == ctypes.sizeof(_lib.MfaFwdParams)
+    assert _lib.MfaFwdParams.workspace.offset == _lib.WORKSPACE_OFFSET
 
 
 def test_invalid_params_rejected_on_host():

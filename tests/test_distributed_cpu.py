@@ -110,6 +110,18 @@ def test_split_kv_merge_over_gloo_matches_unsplit(world, causal):
     assert sorted(covered) == list(range(50))
 
 
+def test_balanced_ranges_equal_causal_work():
+    for L, Lq in ((8192, 8192), (131072, 131072), (5000, 300)):
+        for world in (1, 2, 3, 8):
+            rr = [mfd.balanced_ranges(L, world, r, causal=True, Lq=Lq)[0] for r in range(world)]
+            assert rr[0][0] == 0 and rr[-1][1] == L
+            assert all(a[1] == b[0] for a, b in zip(rr, rr[1:]))
+            work = [attention_pairs(Lq, b - a, True, key_offset=a, lk_total=L) for a, b in rr]
+            assert max(work) - min(work) <= 2 * Lq, (L, world, work)  # a key column per boundary
+        nc = [mfd.balanced_ranges(L, 4, r, causal=False)[0] for r in range(4)]
+        assert [b - a for a, b in nc] == [L // 4] * 4 or sum(b - a for a, b in nc) == L
+
+
 def test_row_shard_partition():
     for Lq in (1, 7, 50, 131072):
         for world in (1, 2, 3, 8):

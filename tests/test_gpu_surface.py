@@ -210,3 +210,47 @@ def test_lse_rescale_sum_kernel_matches_torch():
         assert rc == _lib.OK
         torch.testing.assert_close(out.float(), want, atol=1e-5 if dt == torch.float32 else 2e-2,
                                    rtol=1e-5 if dt == torch.float32 else 1e-2)
+
+
+@pytest.mark.parametrize("ranges", [[(0, 300), (300, 1000)], [(0, 1000)]])
+def test_split_kv_peer_merge_single_rank(nccl_single_rank, ranges):
+    """The peer-memory merge on one rank: the forward scatters its partial rows into the
+    (local) receive buffer, one slot per key chunk, and mfa_lse_merge combines the slots;
+    checked against the oracle and against the NCCL merge."""
+    q, k, v = ref.make_qkv(1, 700, 1000, 4, 2, 128, torch.bfloat16, seed=13)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    kp, vp = [kd[:, a:b] for a, b in ranges], [vd[:, a:b] for a, b in ranges]
+    want = ref.flash_attn_func(q, k, v, causal=True, window_size=(500, -1))
+    outs = {}
+    for merge in ("peer", "nccl"):
+        for _ in range(2):  # the second call reuses the receive buffers
+            out, rows = mfd.flash_attn_split_kv(qd, kp, vp, ranges, 1000, causal=True,
+                                                window_size=(500, -1), merge=merge)
+        assert rows == (0, 700)
+        torch.testing.assert_close(out.float().cpu(), want, atol=2e-2, rtol=2e-2)
+        outs[merge] = out.float()
+    torch.testing.assert_close(outs["peer"], outs["nccl"], atol=8e-3, rtol=1e-2)
+
+
+def test_lse_merge_kernel_matches_torch():
+    from mtlflashattn_b200 import _lib
+    g = torch.Generator(device=DEV).manual_seed(6)
+    n, rows, H, D = 5, 77, 6, 64
+    o = torch.randn(n, rows, H, D, device=DEV, generator=g)
+    lse = torch.randn(n, H, rows, device=DEV, generator=g) * 4
+    lse[1, :, :10] = float("-inf")
+    lse[:, 3, 5] = float("-inf")  # a row no partial attends
+    tot = torch.logsumexp(lse, 0)
+    w = torch.exp(lse - tot).nan_to_num(0.0)
+    want = (w.permute(0, 2, 1)[..., None] * o).sum(0)
+    for dt, code in ((torch.float32, _lib.FP32), (torch.bfloat16, _lib.BF16)):
+        out = torch.empty(rows, H, D, device=DEV, dtype=dt)
+        lo = torch.empty(H, rows, device=DEV)
+        rc = _lib.lse_merge(o.data_ptr(), lse.data_ptr(), n, rows, H, D, out.data_ptr(), code,
+                            lo.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        assert rc == _lib.OK
+        torch.testing.assert_close(out.float(), want, atol=1e-5 if dt == torch.float32 else 2e-2,
+                                   rtol=1e-5 if dt == torch.float32 else 1e-2)
+        fin = torch.isfinite(tot)
+        torch.testing.assert_close(lo[fin], tot[fin])
+        assert torch.isinf(lo[3, 5]) and out[5, 3].abs().max() == 0
