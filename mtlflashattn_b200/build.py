@@ -10,9 +10,9 @@ import os
 import shutil
 import subprocess
 import sys
+import tempfile
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-SRC = os.path.join(HERE, "csrc", "mfa_api.cu")
 OUT = os.path.join(HERE, "libmfa.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -38,22 +38,41 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(s) <= t for s in sources())
 
 
+# Each translation unit with its math flags: the library is built with fast math (the tcgen05
+# kernel's exponentials are ex2.approx by design); the fp32 CUDA-core forward is the accuracy
+# path and is compiled with IEEE division / square root, accurate expf / tanhf / logf and no
+# flush to zero.
+UNITS = (("mfa_api.cu", ["--use_fast_math"]),
+         ("simt_fwd.cu", ["-ftz=false", "-prec-div=true", "-prec-sqrt=true"]))
+
+
 def build(verbose: bool = False, force: bool = False, defines=(), out: str | None = None) -> str:
     """Compile libmfa.so (or, with ``out``, a variant of it at that path; ``defines`` are
     extra NAME=VALUE macros, e.g. the tuning knobs at the top of csrc/fa_sm100.cuh)."""
     target = out or OUT
     if not force and out is None and not defines and up_to_date():
         return OUT
-    cmd = [nvcc_path(), *ARCH, "-O3", "-std=c++17", "-lineinfo", "--use_fast_math",
-           "-Xcompiler", "-fPIC", "-shared", *[f"-D{d}" for d in defines], "-o", target + ".tmp",
-           SRC]
+    base = [nvcc_path(), *ARCH, "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
+            *[f"-D{d}" for d in defines]]
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-    r = subprocess.run(cmd, capture_output=True, text=True)
-    if r.returncode != 0:
-        raise RuntimeError("nvcc failed:\n" + r.stdout + r.stderr)
+        base.insert(1, "-Xptxas=-v")
+    objs = []
+    logs = []
+    with tempfile.TemporaryDirectory() as tmp:
+        for src, flags in UNITS:
+            obj = os.path.join(tmp, src + ".o")
+            r = subprocess.run([*base, *flags, "-c", "-o", obj, os.path.join(HERE, "csrc", src)],
+                               capture_output=True, text=True)
+            if r.returncode != 0:
+                raise RuntimeError(f"nvcc failed on {src}:\n" + r.stdout + r.stderr)
+            logs.append(r.stdout + r.stderr)
+            objs.append(obj)
+        r = subprocess.run([nvcc_path(), *ARCH, "-shared", "-o", target + ".tmp", *objs],
+                           capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("nvcc link failed:\n" + r.stdout + r.stderr)
     if verbose:
-        sys.stderr.write(r.stdout + r.stderr)
+        sys.stderr.write("".join(logs))
     os.replace(target + ".tmp", target)
     return target
 

@@ -16,6 +16,11 @@
 #include "fa_simt.cuh"
 #include "fa_sm100.cuh"
 
+namespace mfa {
+// The fp32 CUDA-core forward, compiled in simt_fwd.cu without fast math.
+int simt_forward(FwdArgs a, int dtype, int D, cudaStream_t st);
+}  // namespace mfa
+
 static_assert(mfa::kMaxPeers == MFA_MAX_PEERS, "peer table size differs from the header's");
 
 namespace mfa {
@@ -515,28 +520,8 @@ int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
 #undef MFA_SM100
 }
 
-template <typename T, int DP>
-int launch_simt(const FwdArgs& a, int64_t grid, cudaStream_t st) {
-  fa_fwd_simt<T, DP><<<(unsigned)grid, simt::kThreads, 0, st>>>(a);
-  return MFA_OK;
-}
-
-int run_simt(const mfa_fwd_params* p, FwdArgs a, cudaStream_t st) {
-  a.num_row_blocks = (a.max_lq + simt::BM - 1) / simt::BM;
-  const int64_t grid = (int64_t)a.num_row_blocks * a.Hq * a.B;
-  if (grid == 0) return MFA_OK;
-  if (grid >= (1ll << 31)) return MFA_ERR_UNSUPPORTED;
-  const int dp = p->D <= 32 ? 32 : (p->D <= 64 ? 64 : 128);
-#define MFA_SIMT(T)                                        \
-  do {                                                     \
-    if (dp == 32) return launch_simt<T, 32>(a, grid, st);  \
-    if (dp == 64) return launch_simt<T, 64>(a, grid, st);  \
-    return launch_simt<T, 128>(a, grid, st);               \
-  } while (0)
-  if (p->dtype == MFA_FP32) MFA_SIMT(float);
-  if (p->dtype == MFA_BF16) MFA_SIMT(__nv_bfloat16);
-  MFA_SIMT(__half);
-#undef MFA_SIMT
+int run_simt(const mfa_fwd_params* p, const FwdArgs& a, cudaStream_t st) {
+  return simt_forward(a, p->dtype, p->D, st) == 0 ? MFA_OK : MFA_ERR_UNSUPPORTED;
 }
 
 // ------------------------------------------------------------------ no-allocation variant
