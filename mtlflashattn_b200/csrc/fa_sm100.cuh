@@ -150,8 +150,12 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 //   kBias = 0  x = s                        (c = scale*log2e folded into the exponent)
 //   kBias = 1  x = log2e*(s*scale - slope*|centre - key|)   (any scale, ALiBi optional)
 //   kBias = 2  x = log2e*(softcap(s*scale) - slope*|centre - key|)
-// Column groups per tile; see the role table above. Measured on B200: the softcap path gains
-// from CG = 2, the plain path loses 9-17%. The ALiBi path (kBias = 1) uses CG = 1 since its
+// Column groups per tile; see the role table above. Measured on B200: the plain path loses 9-17%
+// with CG = 2. The softcap path gained from CG = 2 while its tanh took two MUFU operations;
+// with the hardware tanh, CG = 1 in one-tile CTAs (two per SM) is faster on config 3 (fp16
+// D = 128, softcap 30, window 1024/1024): 447 TFLOP/s (CG 2, two tiles) -> 455 (CG 1, two
+// tiles) -> 504 (CG 1, one tile; 1024 CTAs fill the waves better than 512 and the row max
+// needs no exchange between threads). The ALiBi path (kBias = 1) uses CG = 1 since its
 // bias became two packed FMAs per pair of scores on all but the diagonal blocks (+43% on varlen
 // GQA ALiBi, +55% on dense causal D = 128 ALiBi over CG = 2 with the general bias). Separate
 // kBias = 1 / 2 kernels (rather than one kernel testing softcap at run time) cut the CG = 2
@@ -160,7 +164,7 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 #define MFA_CG_PLAIN 1
 #endif
 #ifndef MFA_CG_SOFTCAP
-#define MFA_CG_SOFTCAP 2
+#define MFA_CG_SOFTCAP 1
 #endif
 #ifndef MFA_CG_LINEAR
 #define MFA_CG_LINEAR 1
@@ -193,9 +197,15 @@ struct DefaultCG {
 #ifndef MFA_TILES128
 #define MFA_TILES128 2
 #endif
-template <int DP, int CG>
+// ... and the softcap kernel at D = 128 (one-tile CTAs: +11% on config 3, above).
+#ifndef MFA_TILES128_SOFTCAP
+#define MFA_TILES128_SOFTCAP 1
+#endif
+template <int DP, int CG, int kBias = 0>
 struct DefaultTiles {
-  static constexpr int value = CG != 1 ? 2 : DP == 64 ? MFA_TILES64 : MFA_TILES128;
+  static constexpr int value = CG != 1 ? 2
+                               : DP == 64 ? MFA_TILES64
+                               : kBias == 2 ? MFA_TILES128_SOFTCAP : MFA_TILES128;
 };
 template <bool B>
 struct BoolC {
@@ -208,7 +218,7 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
 // kPack: the row mapping of decode-like launches (query heads packed per KV head, one-tile CTAs);
 // the other instantiations fold pack_shift to 0 at compile time.
 template <int DP, bool kBF16, int kBias, int CG = DefaultCG<kBias>::value,
-          int TILES = DefaultTiles<DP, CG>::value, bool kPack = false,
+          int TILES = DefaultTiles<DP, CG, kBias>::value, bool kPack = false,
           int kEmu = (kBias == 2 ? MFA_EMU_SOFTCAP
                                  : DP == 64 ? (TILES == 1 ? MFA_EMU64 : 0) : MFA_EMU128),
           int kHalfExp = (kBias == 0 ? (DP == 64 ? MFA_HALF_EXP64 : MFA_HALF_EXP128) : 0)>

@@ -365,7 +365,7 @@ int make_map(CUtensorMap* m, const void* base, int dtype, int D, int H, int64_t 
 // Tiles per CTA of the tcgen05 kernel fa_fwd_sm100<DP, *, GEN> (its default template argument).
 template <int DP, int GEN>
 constexpr int sm100_tiles() {
-  return DefaultTiles<DP, DefaultCG<GEN>::value>::value;
+  return DefaultTiles<DP, DefaultCG<GEN>::value, GEN>::value;
 }
 int sm100_tiles_rt(bool wide, int gen) {
   if (wide) return gen == 2 ? sm100_tiles<128, 2>() : gen == 1 ? sm100_tiles<128, 1>() : sm100_tiles<128, 0>();
