@@ -227,7 +227,7 @@ def _run(p, q, what, causal, trace_shape, kernel, D):
             sel = _lib.select_kernel(p)
             label = "cuda/" + _lib.KERNEL_NAMES.get(sel, "rejected")
             _record_trace(q.dtype, trace_shape[0], trace_shape[1], trace_shape[2], causal, label)
-        stream = torch.cuda.current_stream(dev).cuda_stream
+        stream = torch._C._cuda_getCurrentRawStream(dev.index)  # the current stream's handle
         need = _lib.workspace_size(p)
         if need > 0:  # few query rows: let the library split the keys over more CTAs
             ws = _workspace(dev, stream, need)

@@ -372,9 +372,13 @@ int sm100_tiles_rt(bool wide, int gen) {
   return gen == 2 ? sm100_tiles<64, 2>() : gen == 1 ? sm100_tiles<64, 1>() : sm100_tiles<64, 0>();
 }
 
-// K/V bytes of the (batch, head) pairs whose CTAs run together (see run_sm100).
+// K/V bytes of the (batch, head) pairs whose CTAs run together (see run_sm100). Measured with
+// ncu on B200, B=1 H=16 L=8192 D=128 causal (67 MB of K/V): 64 MB groups (all heads at once)
+// read 137-141 MB of DRAM per launch against 100.7 MB of compulsory Q/K/V, 32 MB groups (8
+// heads) read 100.7 MB, in the same time (263 us). The 126 MB L2 does not keep 67 MB of K/V
+// that every SM reads, so the group budget is a quarter of it.
 #ifndef MFA_L2_GROUP_MB
-#define MFA_L2_GROUP_MB 64
+#define MFA_L2_GROUP_MB 32
 #endif
 
 // SHORT: the one-tile, one-column-group kPack instantiation (sm100_short).
@@ -454,7 +458,7 @@ int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
   a.num_row_blocks = (int)((((int64_t)a.max_lq << a.pack_shift) + rows_per_cta - 1) / rows_per_cta);
   {
     // K/V bytes of one KV head of one sequence; groups of whole KV groups whose K/V stays
-    // within ~64 MB of L2 (all of them when everything fits)
+    // within MFA_L2_GROUP_MB of L2 (all of them when everything fits)
     const int64_t kv_unit = (int64_t)(varlen ? p->max_lk : p->Lk) * p->D * 2 * 2;
     int64_t units = kv_unit > 0 ? ((int64_t)MFA_L2_GROUP_MB << 20) / kv_unit : (1ll << 30);
     if (units < 1) units = 1;
