@@ -83,8 +83,10 @@ class _NoBackward(torch.autograd.Function):
 
 
 def _guard_grad(out, *inputs):
-    if torch.is_grad_enabled() and any(t.requires_grad for t in inputs if torch.is_tensor(t)):
-        return _NoBackward.apply(out, *[t for t in inputs if torch.is_tensor(t)])
+    if torch.is_grad_enabled():
+        ts = [t for t in inputs if torch.is_tensor(t)]
+        if any(t.requires_grad for t in ts):
+            return _NoBackward.apply(out, *ts)
     return out
 
 
@@ -123,7 +125,8 @@ def flash_attn_func(
              if alibi_slopes is not None else None)
     bias = _BiasParams(softcap, window_size[0], window_size[1], alibi)
     out = torch.empty(q.shape, device=q.device, dtype=q.dtype)
-    _kernel.forward_bshd(q.detach(), k.detach(), v.detach(), out, scale, causal, bias)
+    # the kernel reads raw pointers: no autograd graph is recorded, so no detach is needed
+    _kernel.forward_bshd(q, k, v, out, scale, causal, bias)
     return _guard_grad(out, q, k, v)
 
 

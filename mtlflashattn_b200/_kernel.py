@@ -46,8 +46,24 @@ _TIER_ALIASES = {
 }
 
 
+_ENV_DATA = getattr(os.environ, "_data", None)
+
+
+def _env(name, default=""):
+    """os.environ.get for the per-call knobs, without its per-call str -> bytes encoding (the
+    POSIX environ mapping keeps its data keyed by bytes); falls back to os.environ.get."""
+    if _ENV_DATA is not None and os.name == "posix":
+        v = _ENV_DATA.get(name.encode() if name not in _ENV_KEYS else _ENV_KEYS[name])
+        return default if v is None else v.decode()
+    return os.environ.get(name, default)
+
+
+_ENV_KEYS = {n: n.encode() for n in ("MTLFLASHATTN_KERNEL", "MTLFLASHATTN_TRACE",
+                                     "MTLFLASHATTN_SYNC_CHECK")}
+
+
 def _tier_mode(dtype) -> int:
-    raw = os.environ.get("MTLFLASHATTN_KERNEL", "auto").lower()
+    raw = _env("MTLFLASHATTN_KERNEL", "auto").lower()
     if raw in ("torch", "pytorch"):
         raise RuntimeError(
             "mtlflashattn_b200: the chunked-fp32 torch tier is not part of this engine "
@@ -67,7 +83,7 @@ _trace = {}  # (dtype, D, Lq, Lk, causal, label) -> call count
 
 
 def _trace_enabled():
-    return os.environ.get("MTLFLASHATTN_TRACE", "").lower() in ("1", "on", "true", "yes")
+    return _env("MTLFLASHATTN_TRACE").lower() in ("1", "on", "true", "yes")
 
 
 def _record_trace(dtype, D, Lq, Lk, causal, label):
@@ -129,7 +145,7 @@ def check_device_errors(device=None):
 
 
 def _sync_check_enabled():
-    return os.environ.get("MTLFLASHATTN_SYNC_CHECK", "").lower() in ("1", "on", "true", "yes")
+    return _env("MTLFLASHATTN_SYNC_CHECK").lower() in ("1", "on", "true", "yes")
 
 
 # --------------------------------------------------------------------------------- launch
@@ -263,20 +279,28 @@ def forward_bshd(q, k, v, out, scale, causal, bias: _BiasParams, lse=None, k_pos
     (``[B, Lq, Hq, D]``, any strides, fp16/bf16/fp32). ``lse`` is an optional fp32
     ``[B, Hq, Lq]`` tensor. Launches exactly one kernel; no layout copies."""
     _check_tensors(q, k, v)
-    q, k, v = _last_dim_contig(q), _last_dim_contig(k), _last_dim_contig(v)
+    qs, ks, vs, os_ = q.stride(), k.stride(), v.stride(), out.stride()
+    if qs[3] != 1:
+        q = q.contiguous()
+        qs = q.stride()
+    if ks[3] != 1:
+        k = k.contiguous()
+        ks = k.stride()
+    if vs[3] != 1:
+        v = v.contiguous()
+        vs = v.stride()
     B, Lq, Hq, D = q.shape
     Lk, Hkv = k.shape[1], k.shape[2]
     if Hkv == 0 or Hq % Hkv != 0:
         raise ValueError(f"mtlflashattn_b200: num_heads_kv ({Hkv}) must divide num_heads_q ({Hq})")
     if D > MAX_HEAD_DIM:
         raise NotImplementedError(f"mtlflashattn_b200: head_dim {D} > {MAX_HEAD_DIM}")
-    if out.stride(-1) != 1:
+    if os_[3] != 1:
         raise ValueError("mtlflashattn_b200: out must have a contiguous last dimension")
     kernel = _tier_mode(q.dtype)
-    p = _packed(q, k, v, out, B, Hq, Hkv, Lq, Lk, D, q.stride()[:3], k.stride()[:3],
-                v.stride()[:3], out.stride()[:3], scale, causal, bias, kernel, lse,
-                lse.stride()[:2] if lse is not None else (0, 0), None, None, 0, 0,
-                k_pos_offset, lk_total)
+    p = _packed(q, k, v, out, B, Hq, Hkv, Lq, Lk, D, qs[:3], ks[:3], vs[:3], os_[:3], scale,
+                causal, bias, kernel, lse, lse.stride()[:2] if lse is not None else (0, 0), None,
+                None, 0, 0, k_pos_offset, lk_total)
     _run(p, q, "flash_attn_forward", causal, (D, Lq, Lk), kernel, D)
     return out
 
