@@ -44,7 +44,9 @@ enum mfa_status {
   MFA_ERR_TIMEOUT = 4,        /* a bounded in-kernel wait expired; output is invalid */
   MFA_ERR_NO_DEVICE = 5,      /* no usable sm_100 device for the requested kernel */
   MFA_ERR_FAULT_INJECTED = 6, /* host-side fault injection (MFA_FAULT env) fired */
-  MFA_ERR_SCRATCH_TOO_SMALL = 7 /* mfa_fwd_noalloc: the problem needs more than its scratch */
+  MFA_ERR_SCRATCH_TOO_SMALL = 7, /* mfa_fwd_noalloc: the problem needs more than its scratch */
+  MFA_ERR_CHECK = 8             /* (in *err) a device-side bounds check of a build with
+                                   -DMFA_CHECKS=1 failed; the access was skipped */
 };
 
 enum mfa_dtype { MFA_FP16 = 0, MFA_BF16 = 1, MFA_FP32 = 2 };

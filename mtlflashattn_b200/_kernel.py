@@ -140,7 +140,9 @@ def check_device_errors(device=None):
         t.zero_()
         why = ("a kernel gave up on a bounded wait" if v == _lib.ERR_TIMEOUT else
                "a split launch met a varlen row at or past Lq (Lq < cu_seqlens[-1])"
-               if v == _lib.ERR_INVALID else "a kernel reported an error")
+               if v == _lib.ERR_INVALID else
+               "a device-side bounds check (MFA_CHECKS build) failed" if v == _lib.ERR_CHECK
+               else "a kernel reported an error")
         raise _lib.MfaError(v, why + "; its output is invalid")
 
 

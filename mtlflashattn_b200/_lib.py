@@ -24,6 +24,7 @@ ERR_TIMEOUT = 4
 ERR_NO_DEVICE = 5
 ERR_FAULT_INJECTED = 6
 ERR_SCRATCH_TOO_SMALL = 7
+ERR_CHECK = 8
 
 # mfa_dtype
 FP16, BF16, FP32 = 0, 1, 2

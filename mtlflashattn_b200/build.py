@@ -14,6 +14,9 @@ import tempfile
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "libmfa.so")
+# The same library with device-side bounds checks (-DMFA_CHECKS=1): select it with
+# MTLFLASHATTN_LIB to debug a failing shape (a failed check sets MFA_ERR_CHECK, never traps).
+CHECKS_OUT = os.path.join(HERE, "libmfa_checks.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -77,5 +80,15 @@ def build(verbose: bool = False, force: bool = False, defines=(), out: str | Non
     return target
 
 
+def build_checks(force: bool = False) -> str:
+    """Build libmfa_checks.so (the MFA_CHECKS=1 debug variant) next to libmfa.so."""
+    if not force and os.path.exists(CHECKS_OUT) and all(
+            os.path.getmtime(s) <= os.path.getmtime(CHECKS_OUT) for s in sources()):
+        return CHECKS_OUT
+    return build(force=True, defines=("MFA_CHECKS=1",), out=CHECKS_OUT)
+
+
 if __name__ == "__main__":
     print(build(verbose="--verbose" in sys.argv, force=True))
+    if "--checks" in sys.argv:
+        print(build_checks(force=True))

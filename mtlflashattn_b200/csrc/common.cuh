@@ -10,6 +10,14 @@ namespace mfa {
 // Resolved arguments as both kernels read them. Strides are in elements.
 constexpr int kMaxPeers = 8;  // GPUs one split-KV launch can scatter its partial rows to
 
+// Debug build (-DMFA_CHECKS=1): every TMA tile coordinate and every output row address is
+// checked against the launch's extents before use; a failed check stores MFA_ERR_CHECK (8) in
+// the error word, skips the access and ends the CTA's waits (no trap, no fault).
+#ifndef MFA_CHECKS
+#define MFA_CHECKS 0
+#endif
+constexpr int kErrCheck = 8;
+
 struct FwdArgs {
   const void* q;
   const void* k;

@@ -339,8 +339,17 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
     if (n > 0) {
       if (lane == 0) {
         for (int t = 0; t < nt; ++t) {
-          mbar_expect_tx(&q_full[t], C::TILE);
           const int qpos = sv.q0 + ((r0 + t * BM) >> ps);
+          if constexpr (MFA_CHECKS) {
+            const int h_hi = ps ? ((hk + 1) << ps) : hu + 1;  // one past the last head loaded
+            if (qpos < 0 || qpos >= (a.cu_q != nullptr ? a.Lq : sv.lq) || h_hi > a.Hq ||
+                (a.cu_q == nullptr && sv.qb >= a.B)) {
+              if (a.err != nullptr) atomicExch(a.err, kErrCheck);
+              *abort_flag = 1;
+              break;
+            }
+          }
+          mbar_expect_tx(&q_full[t], C::TILE);
           for (int c = 0; c < C::NCH; ++c) {
             if (ps)
               tma_load_4d(sQ + t * C::TILE + c * C::CHUNK, &args.tqp, &q_full[t], 64 * c, hk << ps,
@@ -359,10 +368,20 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
         if (lane == 0) {
           const int j = jb + (it >> 1);
           const CUtensorMap* m = (it & 1) ? &args.tv : &args.tk;
-          mbar_expect_tx(&kv_full[slot], C::TILE);
-          for (int c = 0; c < C::NCH; ++c)
-            tma_load_4d(sKV + slot * C::TILE + c * C::CHUNK, m, &kv_full[slot], 64 * c, hk,
-                        sv.k0 + j * BN, sv.kb);
+          if constexpr (MFA_CHECKS) {
+            const int krow = sv.k0 + j * BN;
+            if (j < 0 || j * BN >= sv.lk || krow < 0 || krow >= a.Lk || hk < 0 || hk >= a.Hkv ||
+                (a.cu_q == nullptr && sv.kb >= a.B)) {
+              if (a.err != nullptr) atomicExch(a.err, kErrCheck);
+              *abort_flag = 1;
+            }
+          }
+          if (!(MFA_CHECKS && *abort_flag)) {
+            mbar_expect_tx(&kv_full[slot], C::TILE);
+            for (int c = 0; c < C::NCH; ++c)
+              tma_load_4d(sKV + slot * C::TILE + c * C::CHUNK, m, &kv_full[slot], 64 * c, hk,
+                          sv.k0 + j * BN, sv.kb);
+          }
         }
         __syncwarp();
       }
@@ -781,6 +800,15 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
       int64_t orow_idx = sv.q0 + row;
       float* lse_base = a.lse;
       uint8_t* obase = reinterpret_cast<uint8_t*>(a.o);
+      if constexpr (MFA_CHECKS) {
+        const bool bad = store && (h < 0 || h >= a.Hq || orow_idx < 0 ||
+                                   (a.peer_n > 0 ? orow_idx >= (int64_t)a.peer_n * a.peer_rows
+                                                 : orow_idx >= (a.cu_q != nullptr ? a.Lq : sv.lq)));
+        if (bad) {
+          if (a.err != nullptr) atomicExch(a.err, kErrCheck);
+          store = false;
+        }
+      }
       if (a.peer_n > 0 && store) {  // the host checked Lq <= peer_n * peer_rows
         const int owner = (int)(orow_idx / a.peer_rows);
         orow_idx -= (int64_t)owner * a.peer_rows;

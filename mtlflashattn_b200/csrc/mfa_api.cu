@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <atomic>
 #include <cstdio>
@@ -22,6 +23,7 @@ int simt_forward(FwdArgs a, int dtype, int D, cudaStream_t st);
 }  // namespace mfa
 
 static_assert(mfa::kMaxPeers == MFA_MAX_PEERS, "peer table size differs from the header's");
+static_assert(mfa::kErrCheck == MFA_ERR_CHECK, "device check status differs from the header's");
 
 namespace mfa {
 namespace {
@@ -42,6 +44,15 @@ bool fault_injected(const char* site) {
   }
   return false;
 }
+
+// ------------------------------------------------------------------ NVTX
+// Host-side range around each launching entry point, named after it, so an nsys / ncu timeline
+// shows which library call queued which kernels. NVTX v3 is header-only: with no tool attached
+// a push/pop is a test of a null function pointer.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+};
 
 // ------------------------------------------------------------------ driver entry point
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -570,6 +581,7 @@ const char* mfa_status_string(int s) {
     case MFA_ERR_TIMEOUT: return "in-kernel wait timed out";
     case MFA_ERR_NO_DEVICE: return "no usable CUDA device";
     case MFA_ERR_FAULT_INJECTED: return "fault injected (MFA_FAULT)";
+    case MFA_ERR_CHECK: return "a device-side check of an MFA_CHECKS build failed";
     case MFA_ERR_SCRATCH_TOO_SMALL:
       return "problem needs more split-KV scratch than mfa_fwd_noalloc's fixed 16 MiB buffer";
     default: return "unknown status";
@@ -613,6 +625,7 @@ int mfa_select_kernel(const mfa_fwd_params* p) {
 
 int mfa_fwd(const mfa_fwd_params* p, void* stream) {
   if (mfa::fault_injected("fwd")) return MFA_ERR_FAULT_INJECTED;
+  mfa::NvtxRange range("mfa_fwd");
   int rc = mfa::validate(p);
   if (rc != MFA_OK) return rc;
   const bool varlen = p->cu_q != nullptr;
@@ -657,6 +670,7 @@ int mfa_fwd_noalloc(const mfa_fwd_params* p, void* stream) {
 
 int mfa_fwd_staged(const mfa_fwd_params* p, const mfa_host_io* io, void* stream) {
   if (mfa::fault_injected("fwd")) return MFA_ERR_FAULT_INJECTED;
+  mfa::NvtxRange range("mfa_fwd_staged");
   if (io == nullptr) return MFA_ERR_INVALID;
   int rc = mfa::validate(p);
   if (rc != MFA_OK) return rc;
@@ -736,6 +750,7 @@ int mfa_lse_rescale_sum(const float* const* o_part, const float* const* lse_part
 
 int mfa_fwd_scatter(const mfa_fwd_params* p, const mfa_peer_scatter* sc, void* stream) {
   if (mfa::fault_injected("fwd")) return MFA_ERR_FAULT_INJECTED;
+  mfa::NvtxRange range("mfa_fwd_scatter");
   if (sc == nullptr) return MFA_ERR_INVALID;
   int rc = mfa::validate(p);
   if (rc != MFA_OK) return rc;
@@ -781,6 +796,7 @@ int mfa_fwd_scatter(const mfa_fwd_params* p, const mfa_peer_scatter* sc, void* s
 int mfa_lse_merge(const float* o_parts, const float* lse_parts, int32_t n, int32_t rows,
                   int32_t H, int32_t D, void* o, int32_t o_dtype, float* lse, void* stream) {
   if (mfa::fault_injected("combine")) return MFA_ERR_FAULT_INJECTED;
+  mfa::NvtxRange range("mfa_lse_merge");
   if (n < 1 || rows < 0 || H < 1 || D < 1 || o_dtype < 0 || o_dtype > 2) return MFA_ERR_INVALID;
   if (rows == 0) return MFA_OK;
   if (o_parts == nullptr || lse_parts == nullptr || o == nullptr) return MFA_ERR_INVALID;
