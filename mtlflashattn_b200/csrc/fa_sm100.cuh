@@ -154,8 +154,8 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 // with CG = 2. The softcap path gained from CG = 2 while its tanh took two MUFU operations;
 // with the hardware tanh, CG = 1 in one-tile CTAs (two per SM) is faster on config 3 (fp16
 // D = 128, softcap 30, window 1024/1024): 447 TFLOP/s (CG 2, two tiles) -> 455 (CG 1, two
-// tiles) -> 504 (CG 1, one tile; 1024 CTAs fill the waves better than 512 and the row max
-// needs no exchange between threads). The ALiBi path (kBias = 1) uses CG = 1 since its
+// tiles) -> 504 (CG 1, one tile; two CTAs per SM issue their MMAs independently and the row
+// max needs no exchange between threads). The ALiBi path (kBias = 1) uses CG = 1 since its
 // bias became two packed FMAs per pair of scores on all but the diagonal blocks (+43% on varlen
 // GQA ALiBi, +55% on dense causal D = 128 ALiBi over CG = 2 with the general bias). Separate
 // kBias = 1 / 2 kernels (rather than one kernel testing softcap at run time) cut the CG = 2
