@@ -433,7 +433,11 @@ def run_gpu(args):
     if world > 1:
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", device_id=dev)
+        import datetime
+
+        # a short collective timeout: a rank that fails in the split-KV leg must not leave the
+        # others waiting for NCCL's default of ten minutes
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=180))
 
     def barrier():
         if dist is not None:
@@ -512,13 +516,23 @@ def run_gpu(args):
     launches = args.steps  # the main timed region: one forward kernel per step
 
     split = None
+    split_failed = False
     if world > 1 and args.config == "5" and not args.no_split_kv:
-        torch.cuda.empty_cache()
-        split = split_kv_leg(min(args.steps, args.split_steps), args.warmup, dev, rank, world,
-                             flush, stream, dist, "peer")
-        torch.cuda.empty_cache()
-        split["nccl_merge"] = split_kv_leg(min(args.steps, args.split_steps), args.warmup, dev,
-                                           rank, world, flush, stream, dist, "nccl")
+        # the headline is already measured: a failure here is reported in the line, not raised
+        for merge in ("peer", "nccl"):
+            torch.cuda.empty_cache()
+            try:
+                leg = split_kv_leg(min(args.steps, args.split_steps), args.warmup, dev, rank,
+                                   world, flush, stream, dist, merge)
+            except Exception as e:  # noqa: BLE001
+                leg = {"merge": merge, "error": f"{type(e).__name__}: {e}"[:300]}
+                split_failed = True
+            if split is None:
+                split = leg
+            else:
+                split["nccl_merge"] = leg
+            if split_failed:
+                break
         torch.cuda.empty_cache()
 
     configs = None
@@ -579,7 +593,7 @@ def run_gpu(args):
             line["split_kv"] = split
         if configs is not None:
             line["configs"] = configs
-    if dist is not None:
+    if dist is not None and not split_failed:  # after a failed collective the group is unusable
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:

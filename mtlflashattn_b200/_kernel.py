@@ -18,6 +18,7 @@ The reference's ``torch`` tier is not part of this engine: that chunked-fp32 alg
 from __future__ import annotations
 
 import atexit
+import collections
 import ctypes
 import os
 import struct
@@ -79,39 +80,47 @@ def _tier_mode(dtype) -> int:
 
 
 # ------------------------------------------------------------------------------------ trace
-_trace = {}  # (dtype, D, Lq, Lk, causal, label) -> call count
+class _CallTrace(collections.Counter):
+    """Per-process tally of forward calls by (dtype, D, Lq, Lk, causal, kernel label), printed
+    to stderr at exit when MTLFLASHATTN_TRACE is on. The line format is the reference's
+    (metal_flash_attn/_kernel.py:1032-1049) because users and scripts read it."""
+
+    def record(self, dtype, D, Lq, Lk, causal, label):
+        """Count one call; a malformed entry is dropped, never raised
+        (reference: _kernel.py:1022-1029)."""
+        try:
+            key = (str(dtype).removeprefix("torch."), int(D), int(Lq), int(Lk), bool(causal),
+                   str(label))
+        except (TypeError, ValueError):
+            return
+        self[key] += 1
+
+    def summary(self):
+        if not self:
+            return []
+        head = (f"[MTLFLASHATTN_TRACE] {sum(self.values())} attention call(s), "
+                f"{len(self)} distinct shape/kernel combos:")
+        body = [f"  calls={n:<6} {dt:<9} D={D:<4} Lq={Lq:<6} Lk={Lk:<6} "
+                f"causal={'T' if causal else 'F'}  -> {label}"
+                for (dt, D, Lq, Lk, causal, label), n in sorted(self.items(),
+                                                                 key=lambda kv: (-kv[1], kv[0]))]
+        return [head, *body]
+
+
+_trace = _CallTrace()
+_record_trace = _trace.record
+_trace_summary_lines = _trace.summary
 
 
 def _trace_enabled():
     return _env("MTLFLASHATTN_TRACE").lower() in ("1", "on", "true", "yes")
 
 
-def _record_trace(dtype, D, Lq, Lk, causal, label):
-    """Count one call per (dtype, D, Lq, Lk, causal, kernel); never raises
-    (reference: _kernel.py:1022-1029)."""
-    try:
-        key = (str(dtype).replace("torch.", ""), int(D), int(Lq), int(Lk), bool(causal), label)
-        _trace[key] = _trace.get(key, 0) + 1
-    except Exception:
-        pass
-
-
-def _trace_summary_lines():
-    if not _trace:
-        return []
-    total = sum(_trace.values())
-    lines = [f"[MTLFLASHATTN_TRACE] {total} attention call(s), "
-             f"{len(_trace)} distinct shape/kernel combos:"]
-    for (dt, D, Lq, Lk, causal, label), n in sorted(_trace.items(), key=lambda kv: (-kv[1], kv[0])):
-        lines.append(f"  calls={n:<6} {dt:<9} D={D:<4} Lq={Lq:<6} Lk={Lk:<6} "
-                     f"causal={'T' if causal else 'F'}  -> {label}")
-    return lines
-
-
 @atexit.register
 def _trace_atexit():
     if _trace_enabled() and _trace:
-        print("\n".join(_trace_summary_lines()), file=sys.stderr, flush=True)
+        sys.stderr.write("\n".join(_trace.summary()) + "\n")
+        sys.stderr.flush()
 
 
 # ------------------------------------------------------------------------ device error word
