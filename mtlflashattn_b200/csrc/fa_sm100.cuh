@@ -62,7 +62,7 @@ constexpr int BN = 128;  // keys per block
 // the registers, under half the shared memory).
 template <int CG, int TILES = 2>
 struct Roles {
-  static_assert(TILES == 2 || CG == 1, "one-tile CTAs use one column group");
+  static_assert(TILES == 2 || CG <= 2, "one-tile CTAs use one or two column groups");
   static constexpr int kSoftWarps = 4 * CG * TILES;
   static constexpr int kProducer = kSoftWarps;
   static constexpr int kMma = kSoftWarps + 1;
@@ -71,8 +71,8 @@ struct Roles {
   // registers per thread at launch: the register file (65536) over the threads of the CTAs
   // that share an SM, rounded down to a multiple of 8
   static constexpr int kLaunchRegs = (65536 / (kThreads * kCtasPerSm)) / 8 * 8;
-  static constexpr int kSoftmaxRegs = TILES == 1 ? 184 : CG == 1 ? 208 : 104;
-  static constexpr int kOtherRegs = TILES == 1 ? 72 : CG == 1 ? 88 : 64;
+  static constexpr int kSoftmaxRegs = TILES == 1 ? (CG == 1 ? 184 : 96) : CG == 1 ? 208 : 104;
+  static constexpr int kOtherRegs = TILES == 1 ? (CG == 1 ? 72 : 48) : CG == 1 ? 88 : 64;
   static constexpr int NC = 128 / CG;  // score columns per softmax thread
   static_assert(TILES * CG * 128 * kSoftmaxRegs + 128 * kOtherRegs <= kThreads * kLaunchRegs,
                 "setmaxnreg split exceeds the launch register budget");
@@ -184,9 +184,20 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b
 #ifndef MFA_PPARTS
 #define MFA_PPARTS 2
 #endif
-template <int kBias>
+// D = 64 (P in its own TMEM columns): 1 = compute all exponentials of a block before waiting for
+// the previous block's P.V (which only the P stores need), 0 = wait first.
+#ifndef MFA_LATE_PV_WAIT
+#define MFA_LATE_PV_WAIT 0
+#endif
+#ifndef MFA_CG_PLAIN64
+#define MFA_CG_PLAIN64 MFA_CG_PLAIN
+#endif
+template <int kBias, int DP = 128>
 struct DefaultCG {
-  static constexpr int value = kBias == 2 ? MFA_CG_SOFTCAP : kBias == 1 ? MFA_CG_LINEAR : MFA_CG_PLAIN;
+  static constexpr int value = kBias == 2   ? MFA_CG_SOFTCAP
+                               : kBias == 1 ? MFA_CG_LINEAR
+                               : DP == 64   ? MFA_CG_PLAIN64
+                                            : MFA_CG_PLAIN;
 };
 // Tiles per CTA: two 128-row tiles share each K/V block in one CTA, except (MFA_TILES64 = 1)
 // D = 64 with one column group, where one-tile CTAs run two per SM. MFA_TILES128 = 1 does the
@@ -201,9 +212,14 @@ struct DefaultCG {
 #ifndef MFA_TILES128_SOFTCAP
 #define MFA_TILES128_SOFTCAP 1
 #endif
+// Two column groups in one-tile D = 64 CTAs (four softmax warps per SM sub-partition) when
+// MFA_TILES64_CG2 = 1.
+#ifndef MFA_TILES64_CG2
+#define MFA_TILES64_CG2 2
+#endif
 template <int DP, int CG, int kBias = 0>
 struct DefaultTiles {
-  static constexpr int value = CG != 1 ? 2
+  static constexpr int value = CG != 1 ? (DP == 64 ? MFA_TILES64_CG2 : 2)
                                : DP == 64 ? MFA_TILES64
                                : kBias == 2 ? MFA_TILES128_SOFTCAP : MFA_TILES128;
 };
@@ -217,7 +233,7 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
 
 // kPack: the row mapping of decode-like launches (query heads packed per KV head, one-tile CTAs);
 // the other instantiations fold pack_shift to 0 at compile time.
-template <int DP, bool kBF16, int kBias, int CG = DefaultCG<kBias>::value,
+template <int DP, bool kBF16, int kBias, int CG = DefaultCG<kBias, DP>::value,
           int TILES = DefaultTiles<DP, CG, kBias>::value, bool kPack = false,
           int kEmu = (kBias == 2 ? MFA_EMU_SOFTCAP
                                  : DP == 64 ? (TILES == 1 ? MFA_EMU64 : 0) : MFA_EMU128),
@@ -682,16 +698,27 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
         named_barrier(1 + t, 256);
         mrow = fmaxf(mrow, *xslot(j & 1, cg ^ 1));
       }
-      if constexpr (C::DECOUPLED) {  // O_t and P_t stay busy until P_t(j-1) V_{j-1} is done
+      // kLate: the exponentials of block j run before the wait for P_t(j-1) V_{j-1}, which
+      // only the P stores (and a rare O rescale) need
+      constexpr bool kLate = C::DECOUPLED && MFA_LATE_PV_WAIT;
+      bool pv_waited = j == 0 || !C::DECOUPLED;
+      if constexpr (C::DECOUPLED && !kLate) {  // O_t, P_t busy until P_t(j-1) V_{j-1} is done
         if (j > 0) {
           ok = __all_sync(kFull, mbar_wait(&pv_done[t], (uint32_t)(j - 1) & 1u, abort_flag));
           if (!ok) break;
           tc_fence_after();
+          pv_waited = true;
         }
       }
       const float m_new = fmaxf(m_used, mrow);
       const bool grow = (m_new - m_used) * c > 8.f;  // false when both are -inf (NaN compare)
       if (__any_sync(kFull, grow)) {  // same rows in both halves -> same decision
+        if (kLate && !pv_waited) {
+          ok = __all_sync(kFull, mbar_wait(&pv_done[t], (uint32_t)(j - 1) & 1u, abort_flag));
+          if (!ok) break;
+          tc_fence_after();
+          pv_waited = true;
+        }
         const float factor = (m_used == -INFINITY) ? 0.f : ex2((m_used - m_new) * c);
         if (j > 0) {
           // O_t is idle here: decoupled, after pv_done; aliased, because the commit that
@@ -716,6 +743,20 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
       // p = 2^(x*c - ref): a fraction kEmu/8 of the pairs on the FMA pipe, the rest on MUFU
       const uint64_t c2 = f2pack(c, c), nref2 = f2pack(-ref, -ref);
       uint64_t acc0 = f2pack(0.f, 0.f), acc1 = acc0;
+      uint32_t pk_all[kLate ? NC / 2 : 1];  // kLate: all of P_t(j) until the stores may start
+      const uint32_t tP = (C::DECOUPLED ? tmem + lane_base + C::TMEM_P + t * 64 : tS) + col0 / 2;
+      auto publish = [&](int cc, const uint32_t* pk) {
+        // P_t: its own columns (decoupled) or over the first 64 columns of S_t
+        tmem_st16(tP + 16 * cc, pk);
+        if constexpr (kPParts > 1) {
+          if ((cc + 1) % (NC / 32 / kPParts) == 0 && cc + 1 < NC / 32) {  // an early part
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[kPParts * t + (cc + 1) / (NC / 32 / kPParts) - 1]);
+          }
+        }
+      };
 #pragma unroll
       for (int cc = 0; cc < NC / 32; ++cc) {  // 32 keys -> 16 packed words per step
         uint32_t pk[16];
@@ -755,16 +796,21 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
           f2unpack(p2, p0, p1);
           pk[i] = pack2<kBF16>(p0, p1);
         }
-        // P_t: its own columns (decoupled) or over the first 64 columns of S_t
-        tmem_st16((C::DECOUPLED ? tmem + lane_base + C::TMEM_P + t * 64 : tS) + col0 / 2 + 16 * cc, pk);
-        if constexpr (kPParts > 1) {
-          if ((cc + 1) % (NC / 32 / kPParts) == 0 && cc + 1 < NC / 32) {  // an early part
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[kPParts * t + (cc + 1) / (NC / 32 / kPParts) - 1]);
-          }
+        if constexpr (kLate) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk_all[16 * cc + i] = pk[i];
+        } else {
+          publish(cc, pk);
         }
+      }
+      if constexpr (kLate) {
+        if (!pv_waited) {
+          ok = __all_sync(kFull, mbar_wait(&pv_done[t], (uint32_t)(j - 1) & 1u, abort_flag));
+          if (!ok) break;
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int cc = 0; cc < NC / 32; ++cc) publish(cc, pk_all + 16 * cc);
       }
       float la, lb;
       f2unpack(fadd2(acc0, acc1), la, lb);

@@ -376,7 +376,7 @@ int make_map(CUtensorMap* m, const void* base, int dtype, int D, int H, int64_t 
 // Tiles per CTA of the tcgen05 kernel fa_fwd_sm100<DP, *, GEN> (its default template argument).
 template <int DP, int GEN>
 constexpr int sm100_tiles() {
-  return DefaultTiles<DP, DefaultCG<GEN>::value, GEN>::value;
+  return DefaultTiles<DP, DefaultCG<GEN, DP>::value, GEN>::value;
 }
 int sm100_tiles_rt(bool wide, int gen) {
   if (wide) return gen == 2 ? sm100_tiles<128, 2>() : gen == 1 ? sm100_tiles<128, 1>() : sm100_tiles<128, 0>();
@@ -395,7 +395,7 @@ int sm100_tiles_rt(bool wide, int gen) {
 // SHORT: the one-tile, one-column-group kPack instantiation (sm100_short).
 template <int DP, bool BF16, int GEN, bool SHORT>
 int launch_sm100(const Sm100Args& args, int dev, int64_t grid, cudaStream_t st) {
-  constexpr int CG = SHORT ? 1 : DefaultCG<GEN>::value;
+  constexpr int CG = SHORT ? 1 : DefaultCG<GEN, DP>::value;
   constexpr int TILES = SHORT ? 1 : sm100_tiles<DP, GEN>();
   auto k = fa_fwd_sm100<DP, BF16, GEN, CG, TILES, SHORT>;
   using R = sm100::Roles<CG, TILES>;
