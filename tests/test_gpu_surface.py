@@ -254,3 +254,47 @@ def test_lse_merge_kernel_matches_torch():
         fin = torch.isfinite(tot)
         torch.testing.assert_close(lo[fin], tot[fin])
         assert torch.isinf(lo[3, 5]) and out[5, 3].abs().max() == 0
+
+
+def test_trace_disabled_records_nothing(monkeypatch):
+    from mtlflashattn_b200 import _kernel
+    monkeypatch.delenv("MTLFLASHATTN_TRACE", raising=False)
+    _kernel._trace.clear()
+    q = torch.randn(1, 2, 64, 64, device=DEV, dtype=torch.float16)
+    _kernel.flash_attn_forward(q, q, q, scale=0.125, causal=False)
+    assert not _kernel._trace
+
+
+def test_trace_records_shape_and_kernel_label(monkeypatch):
+    """Same accounting as the reference's trace (tests/test_trace.py there): one key per
+    (dtype, D, Lq, Lk, causal, kernel), counts accumulate, labels name the kernel that ran."""
+    from mtlflashattn_b200 import _kernel
+    monkeypatch.setenv("MTLFLASHATTN_TRACE", "1")
+    _kernel._trace.clear()
+    q = torch.randn(1, 4, 128, 64, device=DEV, dtype=torch.float16)
+    _kernel.flash_attn_forward(q, q, q, scale=0.125, causal=False)
+    _kernel.flash_attn_forward(q, q, q, scale=0.125, causal=False)
+    qf = torch.randn(1, 2, 96, 32, device=DEV, dtype=torch.float32)
+    _kernel.flash_attn_forward(qf, qf, qf, scale=0.2, causal=True)
+    assert _kernel._trace[("float16", 64, 128, 128, False, "cuda/tcgen05")] == 2
+    assert _kernel._trace[("float32", 32, 96, 96, True, "cuda/simt")] == 1
+    lines = _kernel._trace_summary_lines()
+    assert lines[0].startswith("[MTLFLASHATTN_TRACE] 3 attention call(s), 2 distinct")
+    _kernel._trace.clear()
+
+
+def test_trace_summary_printed_at_exit():
+    import subprocess
+    import sys
+    root = os.path.dirname(HERE) if "HERE" in globals() else os.path.dirname(os.path.dirname(
+        os.path.abspath(__file__)))
+    code = ("import torch, mtlflashattn_b200 as m\n"
+            "q = torch.randn(1, 256, 4, 64, device='cuda', dtype=torch.bfloat16)\n"
+            "m.flash_attn_func(q, q, q, causal=True); torch.cuda.synchronize()\n")
+    env = dict(os.environ, MTLFLASHATTN_TRACE="1",
+               PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "[MTLFLASHATTN_TRACE] 1 attention call(s)" in r.stderr
+    assert "-> cuda/tcgen05" in r.stderr
