@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define MFA_ABI_VERSION 6
+#define MFA_ABI_VERSION 7
 
 /* Status codes. The Python layer maps them to the reference's exception types. */
 enum mfa_status {
@@ -97,6 +97,10 @@ typedef struct mfa_fwd_params {
    * mfa_fwd_workspace_size; NULL or too small simply disables the split. */
   void* workspace;
   size_t workspace_bytes;
+  /* varlen, optional: a HOST copy of cu_q ([B + 1]). With it (and B <= 256) the launch runs
+   * exactly the CTAs the sequences need, longest sequence first, instead of max_lq's row
+   * blocks for every sequence with the surplus CTAs exiting at once. */
+  const int32_t* cu_q_host;
 } mfa_fwd_params;
 
 /* Attention forward. Replaces the tier dispatch under flash_attn_forward

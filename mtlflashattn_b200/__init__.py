@@ -203,8 +203,8 @@ def flash_attn_varlen_func(
     bias = _BiasParams(softcap, window_size[0], window_size[1], alibi)
     cu_q_dev = _as_cu(cu_seqlens_q, q.device)
     cu_k_dev = _as_cu(cu_seqlens_k, q.device)
-    _kernel.forward_varlen(q.detach(), k.detach(), v.detach(), out, cu_q_dev, cu_k_dev,
-                           max(lens_q), max(lens_k), scale, causal, bias)
+    _kernel.forward_varlen(q, k, v, out, cu_q_dev, cu_k_dev, max(lens_q), max(lens_k), scale,
+                           causal, bias, cu_q_host=cu_q)
     return _guard_grad(out, q, k, v)
 
 

@@ -17,6 +17,7 @@ The reference's ``torch`` tier is not part of this engine: that chunked-fp32 alg
 """
 from __future__ import annotations
 
+import array
 import atexit
 import collections
 import ctypes
@@ -192,7 +193,8 @@ _tls = threading.local()
 
 
 def _values(q, k, v, o, B, Hq, Hkv, Lq, Lk, D, q_st, k_st, v_st, o_st, scale, causal, bias,
-            kernel, lse, lse_st, cu_q, cu_k, max_lq, max_lk, k_pos_offset, lk_total):
+            kernel, lse, lse_st, cu_q, cu_k, max_lq, max_lk, k_pos_offset, lk_total,
+            cu_q_host=0):
     """The fields of ``struct mfa_fwd_params`` in declaration order (workspace left empty)."""
     return (q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
             lse.data_ptr() if lse is not None else 0,
@@ -204,7 +206,7 @@ def _values(q, k, v, o, B, Hq, Hkv, Lq, Lk, D, q_st, k_st, v_st, o_st, scale, ca
             int(bias.window_left), int(bias.window_right),
             bias.alibi.data_ptr() if bias.alibi is not None else 0,
             _DTYPES[q.dtype], _DTYPES[o.dtype], int(k_pos_offset), int(lk_total), kernel,
-            _err_word(q.device).data_ptr(), 0, 0)
+            _err_word(q.device).data_ptr(), 0, 0, cu_q_host)
 
 
 def _params(q, k, v, o, *, B, Hq, Hkv, Lq, Lk, D, q_st, k_st, v_st, o_st, scale, causal,
@@ -215,6 +217,19 @@ def _params(q, k, v, o, *, B, Hq, Hkv, Lq, Lk, D, q_st, k_st, v_st, o_st, scale,
     vals = _values(q, k, v, o, B, Hq, Hkv, Lq, Lk, D, q_st, k_st, v_st, o_st, scale, causal,
                    bias, kernel, lse, lse_st, cu_q, cu_k, max_lq, max_lk, k_pos_offset, lk_total)
     return _lib.MfaFwdParams.from_buffer_copy(_PACK.pack(*vals))
+
+
+_tls_host = threading.local()
+
+
+def _host_i32(values):
+    """Address of a host int32 copy of ``values`` (0 for None), valid until the next call on
+    this thread."""
+    if values is None:
+        return 0
+    arr = array.array("i", values)
+    _tls_host.keep = arr
+    return arr.buffer_info()[0]
 
 
 def _packed(*args):
@@ -317,10 +332,11 @@ def forward_bshd(q, k, v, out, scale, causal, bias: _BiasParams, lse=None, k_pos
 
 
 def forward_varlen(q, k, v, out, cu_q, cu_k, max_lq, max_lk, scale, causal, bias: _BiasParams,
-                   lse=None):
+                   lse=None, cu_q_host=None):
     """Packed varlen attention in ONE launch: q ``[total_q, Hq, D]``, k/v ``[total_k, Hkv, D]``,
     device int32 ``cu_q``/``cu_k`` ``[batch+1]``; ``bias.alibi`` is ``[batch*Hq]`` or None.
-    ``lse`` is an optional fp32 ``[Hq, total_q]`` tensor."""
+    ``lse`` is an optional fp32 ``[Hq, total_q]`` tensor. ``cu_q_host``, the same offsets as a
+    host list, lets the library launch exactly the CTAs the sequences need."""
     _check_tensors(q, k, v)
     q, k, v = _last_dim_contig(q), _last_dim_contig(k), _last_dim_contig(v)
     total_q, Hq, D = q.shape
@@ -331,7 +347,7 @@ def forward_varlen(q, k, v, out, cu_q, cu_k, max_lq, max_lk, scale, causal, bias
                 (0, k.stride(0), k.stride(1)), (0, v.stride(0), v.stride(1)),
                 (0, out.stride(0), out.stride(1)), scale, causal, bias, kernel, lse,
                 (0, lse.stride(0)) if lse is not None else (0, 0), cu_q, cu_k, max_lq, max_lk,
-                0, 0)
+                0, 0, _host_i32(cu_q_host))
     _run(p, q, "flash_attn_varlen_func", causal, (D, max_lq, max_lk), kernel, D)
     return out
 

@@ -13,7 +13,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmfa.so")
 
-MFA_ABI_VERSION = 6
+MFA_ABI_VERSION = 7
 
 # mfa_status
 OK = 0
@@ -94,6 +94,7 @@ class MfaFwdParams(ctypes.Structure):
         ("err", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("cu_q_host", ctypes.c_void_p),
     ]
 
 
@@ -101,7 +102,7 @@ class MfaFwdParams(ctypes.Structure):
 # the hot path fills a reusable buffer with one pack_into call instead of ~40 ctypes field
 # assignments (about 1.5 us against 8 us per forward). The offsets of the two workspace fields
 # let a caller patch them after sizing the workspace.
-PARAMS_FORMAT = "<5Q12q2q6i2Q2i2f3i4xQ5i4xQQQ"
+PARAMS_FORMAT = "<5Q12q2q6i2Q2i2f3i4xQ5i4xQQQQ"
 WORKSPACE_OFFSET = 264  # workspace pointer, then workspace_bytes
 
 

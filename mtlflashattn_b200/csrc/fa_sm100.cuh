@@ -45,11 +45,22 @@
 
 namespace mfa {
 
+// Exact CTA list of a varlen launch whose sequence lengths the host knows (n > 0): sequences in
+// the order seq[0..n), longest first; sequence seq[i] owns CTAs [off[i], off[i+1]) of the grid,
+// its row blocks x heads x splits and nothing else, so no CTA lands past a sequence's last row.
+constexpr int kMaxTileSeqs = 256;
+struct TileList {
+  int n;
+  int seq[kMaxTileSeqs];
+  int off[kMaxTileSeqs + 1];
+};
+
 struct Sm100Args {
   CUtensorMap tq, tk, tv;  // 4-D maps (D, H, S, B), box (64, 1, 128, 1), 128B swizzle
   // head-packed query map: box (64, 2^pack_shift, 128 >> pack_shift, 1), rows head-fastest
   CUtensorMap tqp;
   FwdArgs a;
+  TileList tl;
 };
 
 namespace sm100 {
@@ -275,21 +286,43 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
   // ---- work decode: heaviest row blocks first across all (batch, head)
   // (groups of (batch, head) pairs whose K/V fits in L2, one after the other)
   const int idx = blockIdx.x;
-  const int per_group = a.num_row_blocks * a.group_hb * a.num_splits;
-  const int grp = idx / per_group;
-  const int hb0 = grp * a.group_hb;
   // head-packed: one CTA per (batch, KV head); tile row r is position r >> ps of query head
   // (hk << ps) + (r & pmask). Unpacked (ps = 0): one CTA per (batch, query head), r = position.
   const int ps = kPack ? a.pack_shift : 0;
   const int pmask = (1 << ps) - 1;
   const int heads = a.Hq >> ps;
-  const int GHS = min(a.group_hb, heads * a.B - hb0) * a.num_splits;  // CTAs per row block
-  const int ri = idx - grp * per_group;
-  const int rb = a.num_row_blocks - 1 - ri / GHS;
-  const int split = (ri % GHS) % a.num_splits;  // splits of one row block run side by side
-  const int hb = hb0 + (ri % GHS) / a.num_splits;
-  const int hu = hb % heads;  // query head, or KV head when packed
-  const int b = hb / heads;
+  int rb, split, hu, b;
+  if (args.tl.n > 0) {
+    // exact varlen list: find the sequence, then within it groups of group_hb heads (L2), each
+    // group's row blocks heaviest first, the splits of a row block side by side
+    int lo = 0, hi = args.tl.n - 1;
+    while (lo < hi) {  // the last i with off[i] <= idx
+      const int mid = (lo + hi + 1) >> 1;
+      if (args.tl.off[mid] <= idx) lo = mid; else hi = mid - 1;
+    }
+    b = args.tl.seq[lo];
+    const int ri0 = idx - args.tl.off[lo];
+    const int nrb = (args.tl.off[lo + 1] - args.tl.off[lo]) / (heads * a.num_splits);
+    const int gh = min(a.group_hb, heads);
+    const int per_full = nrb * gh * a.num_splits;
+    const int g = ri0 / per_full;
+    const int gsz = min(gh, heads - g * gh) * a.num_splits;  // CTAs per row block in group g
+    const int ri = ri0 - g * per_full;
+    rb = nrb - 1 - ri / gsz;
+    split = (ri % gsz) % a.num_splits;
+    hu = g * gh + (ri % gsz) / a.num_splits;
+  } else {
+    const int per_group = a.num_row_blocks * a.group_hb * a.num_splits;
+    const int grp = idx / per_group;
+    const int hb0 = grp * a.group_hb;
+    const int GHS = min(a.group_hb, heads * a.B - hb0) * a.num_splits;  // CTAs per row block
+    const int ri = idx - grp * per_group;
+    rb = a.num_row_blocks - 1 - ri / GHS;
+    split = (ri % GHS) % a.num_splits;  // splits of one row block run side by side
+    const int hb = hb0 + (ri % GHS) / a.num_splits;
+    hu = hb % heads;  // query head, or KV head when packed
+    b = hb / heads;
+  }
   const int hk = ps ? hu : hu / a.group;
   const SeqView sv = seq_view(a, b);
   const int rows = sv.lq << ps;  // tile rows of this (batch, head unit)

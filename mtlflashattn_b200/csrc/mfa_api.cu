@@ -6,6 +6,7 @@
 #include <cudaTypedefs.h>
 #include <nvtx3/nvToolsExt.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
@@ -503,7 +504,31 @@ int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
     a.lse_split_stride = rows;
   }
   args.a = a;
-  const int64_t grid = (int64_t)a.num_row_blocks * heads * a.B * a.num_splits;
+  int64_t grid = (int64_t)a.num_row_blocks * heads * a.B * a.num_splits;
+  if (varlen && p->cu_q_host != nullptr && p->B <= kMaxTileSeqs) {
+    // exact CTA list: each non-empty sequence's row blocks x heads x splits, longest first
+    struct SeqBlocks {
+      int seq, nrb;
+    };
+    SeqBlocks sb[kMaxTileSeqs];
+    int n = 0;
+    for (int i = 0; i < p->B; ++i) {
+      const int64_t rows = (int64_t)(p->cu_q_host[i + 1] - p->cu_q_host[i]) << a.pack_shift;
+      if (rows <= 0) continue;  // no query rows: nothing to compute or write
+      sb[n++] = SeqBlocks{i, (int)((rows + rows_per_cta - 1) / rows_per_cta)};
+    }
+    std::stable_sort(sb, sb + n, [](const SeqBlocks& x, const SeqBlocks& y) { return x.nrb > y.nrb; });
+    args.tl.n = n;
+    args.tl.off[0] = 0;
+    int64_t total = 0;
+    for (int i = 0; i < n; ++i) {
+      args.tl.seq[i] = sb[i].seq;
+      total += (int64_t)sb[i].nrb * heads * a.num_splits;
+      if (total >= (1ll << 31)) return MFA_ERR_UNSUPPORTED;
+      args.tl.off[i + 1] = (int)total;
+    }
+    grid = total;
+  }
   if (grid == 0) return MFA_OK;
   if (grid >= (1ll << 31)) return MFA_ERR_UNSUPPORTED;
   const bool bf = p->dtype == MFA_BF16;
