@@ -89,22 +89,39 @@ struct Roles {
                 "setmaxnreg split exceeds the launch register budget");
 };
 
-template <int DP, int TILES = 2>
+// KBN keys per K/V block (128; 64 for the MFA_BN64_D128 variant of the D = 128 plain kernel).
+template <int DP, int TILES = 2, int KBN = 128>
 struct Cfg {
   static constexpr int NCH = DP / 64;                    // 128-byte column chunks per row
-  static constexpr uint32_t CHUNK = 128u * 128u;         // one chunk of 128 rows: 16 KB
-  static constexpr uint32_t TILE = NCH * CHUNK;          // Q tile or K / V block
-  static constexpr int NSLOT = DP == 128 ? (TILES == 1 ? 2 : 3) : TILES == 1 ? 5 : 6;  // K/V ring
-  static constexpr uint32_t BAR_OFF = TILES * TILE + NSLOT * TILE;
+  static constexpr uint32_t CHUNK = 128u * 128u;         // one Q chunk of 128 rows: 16 KB
+  static constexpr uint32_t TILE = NCH * CHUNK;          // Q tile
+  static constexpr uint32_t KCHUNK = (uint32_t)KBN * 128u;  // one K / V chunk of KBN rows
+  static constexpr uint32_t KTILE = NCH * KCHUNK;        // K / V block
+  static constexpr int NSLOT = KBN == 64 ? 8
+                               : DP == 128 ? (TILES == 1 ? 2 : 3) : TILES == 1 ? 5 : 6;  // ring
+  static constexpr uint32_t BAR_OFF = TILES * TILE + NSLOT * KTILE;
   static constexpr uint32_t XCH_OFF = BAR_OFF + 256;     // [parity][tile][cg][row] fp32 (CG = 2)
-  // TMEM columns: S_t at 128 t, O_t at TMEM_O + DP t, and (decoupled) P_t at TMEM_P + 64 t.
-  // D = 64 leaves room for P in its own columns and S is released to the MMA as soon as it is
-  // in registers (see "decoupled" below). D = 128 aliases P over S.
-  static constexpr bool DECOUPLED = DP == 64;
-  static constexpr uint32_t TMEM_O = 128u * TILES;
-  static constexpr uint32_t TMEM_P = 128u * TILES + (uint32_t)DP * TILES;
+  // TMEM columns: S_t at KBN t, O_t at TMEM_O + DP t, and (decoupled) P_t at TMEM_P + KBN/2 t.
+  // D = 64 (and D = 128 with 64-key blocks) leaves room for P in its own columns and S is
+  // released to the MMA as soon as it is in registers (see "decoupled" below). Otherwise P
+  // aliases S.
+  static constexpr bool DECOUPLED = DP == 64 || KBN == 64;
+  static constexpr uint32_t TMEM_S = (uint32_t)KBN;      // columns of one tile's S
+  static constexpr uint32_t TMEM_O = (uint32_t)KBN * TILES;
+  static constexpr uint32_t TMEM_P = (uint32_t)KBN * TILES + (uint32_t)DP * TILES;
   static constexpr uint32_t TMEM_COLS = TILES == 1 ? 256 : 512;
+  static_assert(!DECOUPLED || TMEM_P + (uint32_t)(KBN / 2) * TILES <= TMEM_COLS, "TMEM plan");
   static constexpr uint32_t SMEM = XCH_OFF + 4096 + 1024;  // + alignment slack
+};
+
+// Keys per K/V block of an instantiation (host and device agree through this).
+#ifndef MFA_BN64_D128
+#define MFA_BN64_D128 0
+#endif
+template <int DP, int kBias, int CG, int TILES, bool kPack>
+struct BlockKeys {
+  static constexpr int value =
+      (MFA_BN64_D128 && DP == 128 && kBias == 0 && CG == 1 && TILES == 2 && !kPack) ? 64 : 128;
 };
 
 // Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.
@@ -253,11 +270,12 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
                                   sm100::Roles<CG, TILES>::kCtasPerSm)
     fa_fwd_sm100(const __grid_constant__ Sm100Args args) {
   using namespace sm100;
-  using C = Cfg<DP, TILES>;
+  constexpr int KBN = BlockKeys<DP, kBias, CG, TILES, kPack>::value;
+  using C = Cfg<DP, TILES, KBN>;
   using R = Roles<CG, TILES>;
   constexpr int kSoftmaxRegs = R::kSoftmaxRegs;
   constexpr int kOtherRegs = R::kOtherRegs;
-  constexpr int NC = R::NC;
+  constexpr int NC = KBN / CG;  // score columns per softmax thread
   // P_t is published to the MMA in this many key parts (one part with CG = 2, where both
   // column groups' halves are needed before the P.V MMAs of a part could start anyway).
   constexpr int kPParts = CG == 1 ? MFA_PPARTS : 1;
@@ -268,7 +286,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* sb = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* sQ = sb;
-  uint8_t* sKV = sb + TILES * C::TILE;
+  uint8_t* sKV = sb + TILES * C::TILE;  // K / V ring: NSLOT blocks of C::KTILE
   uint64_t* bars = reinterpret_cast<uint64_t*>(sb + C::BAR_OFF);
   uint64_t* q_full = bars;                 // [2]
   uint64_t* kv_full = bars + 2;            // [NSLOT]
@@ -342,8 +360,8 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
     klo = max(klo, split * a.split_keys);
     if (split + 1 < a.num_splits) khi = min(khi, (split + 1) * a.split_keys);
   }
-  const int jb = klo / BN;
-  const int n = khi > klo ? (khi + BN - 1) / BN - jb : 0;
+  const int jb = klo / KBN;
+  const int n = khi > klo ? (khi + KBN - 1) / KBN - jb : 0;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -418,18 +436,18 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
           const int j = jb + (it >> 1);
           const CUtensorMap* m = (it & 1) ? &args.tv : &args.tk;
           if constexpr (MFA_CHECKS) {
-            const int krow = sv.k0 + j * BN;
-            if (j < 0 || j * BN >= sv.lk || krow < 0 || krow >= a.Lk || hk < 0 || hk >= a.Hkv ||
+            const int krow = sv.k0 + j * KBN;
+            if (j < 0 || j * KBN >= sv.lk || krow < 0 || krow >= a.Lk || hk < 0 || hk >= a.Hkv ||
                 (a.cu_q == nullptr && sv.kb >= a.B)) {
               if (a.err != nullptr) atomicExch(a.err, kErrCheck);
               *abort_flag = 1;
             }
           }
           if (!(MFA_CHECKS && *abort_flag)) {
-            mbar_expect_tx(&kv_full[slot], C::TILE);
+            mbar_expect_tx(&kv_full[slot], C::KTILE);
             for (int c = 0; c < C::NCH; ++c)
-              tma_load_4d(sKV + slot * C::TILE + c * C::CHUNK, m, &kv_full[slot], 64 * c, hk,
-                          sv.k0 + j * BN, sv.kb);
+              tma_load_4d(sKV + slot * C::KTILE + c * C::KCHUNK, m, &kv_full[slot], 64 * c, hk,
+                          sv.k0 + j * KBN, sv.kb);
           }
         }
         __syncwarp();
@@ -439,7 +457,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
     // ------------------------------------------------------------ MMA issuer (one thread)
     regs_dec<kOtherRegs>();
     if (n > 0 && lane == 0) {
-      constexpr uint32_t kIdQK = idesc_f16(kBF16, BM, BN, false);
+      constexpr uint32_t kIdQK = idesc_f16(kBF16, BM, KBN, false);
       constexpr uint32_t kIdPV = idesc_f16(kBF16, BM, DP, true);
       const uint32_t sQa = smem_u32(sQ);
       const uint32_t sKVa = smem_u32(sKV);
@@ -448,29 +466,30 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
       // them per MMA made the single issuing thread, not the tensor pipe, the bottleneck.
       const uint64_t dQ = desc_sw128(sQa, 16, 1024);
       const uint64_t dK = desc_sw128(sKVa, 16, 1024);
-      const uint64_t dV = desc_sw128(sKVa, C::CHUNK, 1024);
+      const uint64_t dV = desc_sw128(sKVa, C::KCHUNK, 1024);
       auto qk = [&](int t, int it) {  // S_t = Q_t K^T, K in ring item `it`
         const uint64_t a0 = dQ + ((t * C::TILE) >> 4);
-        const uint64_t b0 = dK + (((it % C::NSLOT) * C::TILE) >> 4);
-        const uint32_t d = tmem + 128u * t;
+        const uint64_t b0 = dK + (((it % C::NSLOT) * C::KTILE) >> 4);
+        const uint32_t d = tmem + C::TMEM_S * t;
 #pragma unroll
         for (int k = 0; k < DP / 16; ++k) {
-          const uint32_t koff = ((k >> 2) * C::CHUNK + (k & 3) * 32) >> 4;
-          mma_ss(d, a0 + koff, b0 + koff, kIdQK, k > 0);
+          const uint32_t koff_a = ((k >> 2) * C::CHUNK + (k & 3) * 32) >> 4;
+          const uint32_t koff_b = ((k >> 2) * C::KCHUNK + (k & 3) * 32) >> 4;
+          mma_ss(d, a0 + koff_a, b0 + koff_b, kIdQK, k > 0);
         }
       };
       // O_t (+)= P_t V, V in ring item `it`. P_t arrives in kPParts key parts; the MMAs of a
       // part run while the softmax is still producing the next one.
       auto pv = [&](int t, int it, bool acc, int j) {
-        const uint64_t b0 = dV + (((it % C::NSLOT) * C::TILE) >> 4);
+        const uint64_t b0 = dV + (((it % C::NSLOT) * C::KTILE) >> 4);
         const uint32_t d = tmem + C::TMEM_O + DP * t;
-        const uint32_t pa = tmem + (C::DECOUPLED ? C::TMEM_P + 64u * t : 128u * t);
+        const uint32_t pa = tmem + (C::DECOUPLED ? C::TMEM_P + (KBN / 2) * t : C::TMEM_S * t);
 #pragma unroll
         for (int q = 0; q < kPParts; ++q) {
           if (!mbar_wait(&p_full[kPParts * t + q], (uint32_t)j & 1u, abort_flag)) return false;
           tc_fence_after();
 #pragma unroll
-          for (int k = q * (8 / kPParts); k < (q + 1) * (8 / kPParts); ++k)
+          for (int k = q * (KBN / 16 / kPParts); k < (q + 1) * (KBN / 16 / kPParts); ++k)
             mma_ts(d, pa + k * 8, b0 + ((k * 2048) >> 4), kIdPV, (acc || k > 0) ? 1u : 0u);
         }
         return true;
@@ -575,7 +594,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
     const int h = ps ? (hk << ps) + (trow & pmask) : hu;  // query head of this row
     const int nj = (TILES == 1 || t < nt) ? n : 0;  // key blocks this tile runs (0: empty tile)
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
-    const uint32_t tS = tmem + lane_base + t * 128;
+    const uint32_t tS = tmem + lane_base + C::TMEM_S * t;
     const uint32_t tO = tmem + lane_base + C::TMEM_O + t * DP;
     const KeyRange kr = key_range(a, sv, row);
     // tile-uniform interval extremes for the "block needs no mask" test
@@ -615,8 +634,8 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
         if (lane == 0) mbar_arrive(&s_free[t]);
       }
       float x[NC];
-      const int c0 = (jb + j) * BN + col0;  // local key index of x[0]
-      const bool need_mask = ((jb + j) * BN < tile_lo_max) || ((jb + j) * BN + BN > tile_hi_min);
+      const int c0 = (jb + j) * KBN + col0;  // local key index of x[0]
+      const bool need_mask = ((jb + j) * KBN < tile_lo_max) || ((jb + j) * KBN + KBN > tile_hi_min);
       // ALiBi on a block whose keys all lie on one side of the centre of every row of this
       // warp (every causal block but the diagonal): |centre - key| is linear in the key index,
       // so the bias is one packed FMA, slope' * i + base, and x = s * scale + bias another.
@@ -777,7 +796,7 @@ __global__ void __launch_bounds__(sm100::Roles<CG, TILES>::kThreads,
       const uint64_t c2 = f2pack(c, c), nref2 = f2pack(-ref, -ref);
       uint64_t acc0 = f2pack(0.f, 0.f), acc1 = acc0;
       uint32_t pk_all[kLate ? NC / 2 : 1];  // kLate: all of P_t(j) until the stores may start
-      const uint32_t tP = (C::DECOUPLED ? tmem + lane_base + C::TMEM_P + t * 64 : tS) + col0 / 2;
+      const uint32_t tP = (C::DECOUPLED ? tmem + lane_base + C::TMEM_P + t * (KBN / 2) : tS) + col0 / 2;
       auto publish = [&](int cc, const uint32_t* pk) {
         // P_t: its own columns (decoupled) or over the first 64 columns of S_t
         tmem_st16(tP + 16 * cc, pk);

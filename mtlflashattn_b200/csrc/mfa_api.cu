@@ -294,7 +294,8 @@ int pick_kernel(const mfa_fwd_params* p, int dev) {
 
 // 4-D tensor map over (D, H, S, B) with a (64, 1, 128, 1) box and 128-byte swizzle.
 int encode_map(CUtensorMap* m, const void* base, int dtype, int D, int H, int64_t S, int B,
-             const int64_t* stride /* batch, seq, head (elements) */, int box_h = 1) {
+             const int64_t* stride /* batch, seq, head (elements) */, int box_h = 1,
+             int rows = 128) {
   auto fn = encode_fn();
   if (fn == nullptr) return MFA_ERR_CUDA;
   const int64_t es = 2;
@@ -306,7 +307,7 @@ int encode_map(CUtensorMap* m, const void* base, int dtype, int D, int H, int64_
   if (S <= 1) ss = 16;
   if (B <= 1) sbt = 16;
   cuuint64_t strides[3] = {(cuuint64_t)sh, (cuuint64_t)ss, (cuuint64_t)sbt};
-  cuuint32_t box[4] = {64, (cuuint32_t)box_h, (cuuint32_t)(128 / box_h), 1};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_h, (cuuint32_t)(rows / box_h), 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(m, dtype == MFA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                   4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -323,11 +324,11 @@ int encode_map(CUtensorMap* m, const void* base, int dtype, int D, int H, int64_
 struct MapKey {
   const void* base;
   int64_t S, stride[3];
-  int dtype, D, H, B, box_h;
+  int dtype, D, H, B, box_h, rows;
   bool operator==(const MapKey& o) const {
     return base == o.base && S == o.S && stride[0] == o.stride[0] && stride[1] == o.stride[1] &&
            stride[2] == o.stride[2] && dtype == o.dtype && D == o.D && H == o.H && B == o.B &&
-           box_h == o.box_h;
+           box_h == o.box_h && rows == o.rows;
   }
 };
 constexpr int kMapSlots = 256;
@@ -338,7 +339,7 @@ struct MapSlot {
 };
 
 int make_map(CUtensorMap* m, const void* base, int dtype, int D, int H, int64_t S, int B,
-             const int64_t* stride, int box_h = 1) {
+             const int64_t* stride, int box_h = 1, int rows = 128) {
   static std::mutex mu;
   static MapSlot slots[kMapSlots];
   MapKey key;
@@ -353,8 +354,10 @@ int make_map(CUtensorMap* m, const void* base, int dtype, int D, int H, int64_t 
   key.H = H;
   key.B = B;
   key.box_h = box_h;
+  key.rows = rows;
   uint64_t h = reinterpret_cast<uintptr_t>(base) >> 4;
-  const int64_t mix[8] = {S, stride[0], stride[1], stride[2], dtype, D, H, (int64_t)B * 64 + box_h};
+  const int64_t mix[8] = {S, stride[0], stride[1], stride[2], dtype, D, H,
+                          ((int64_t)B * 64 + box_h) * 512 + rows};
   for (int i = 0; i < 8; ++i) h = (h ^ (uint64_t)mix[i]) * 0x100000001b3ull;
   MapSlot& sl = slots[(h ^ (h >> 29)) % kMapSlots];
   {
@@ -364,7 +367,7 @@ int make_map(CUtensorMap* m, const void* base, int dtype, int D, int H, int64_t 
       return MFA_OK;
     }
   }
-  const int rc = encode_map(m, base, dtype, D, H, S, B, stride, box_h);
+  const int rc = encode_map(m, base, dtype, D, H, S, B, stride, box_h, rows);
   if (rc == MFA_OK) {
     std::lock_guard<std::mutex> g(mu);
     sl.used = true;
@@ -393,6 +396,23 @@ int sm100_tiles_rt(bool wide, int gen) {
 #define MFA_L2_GROUP_MB 32
 #endif
 
+// Keys per K/V block of the instantiation launch_sm100 will pick (BlockKeys on the host).
+template <int DP, int GEN, bool SHORT>
+constexpr int sm100_kbn() {
+  return SHORT ? sm100::BlockKeys<DP, GEN, 1, 1, true>::value
+               : sm100::BlockKeys<DP, GEN, DefaultCG<GEN, DP>::value, sm100_tiles<DP, GEN>(),
+                                        false>::value;
+}
+int sm100_kbn_rt(bool wide, int gen, bool short_rows) {
+#define MFA_KBN(DP)                                                                          \
+  (short_rows ? (gen == 2 ? sm100_kbn<DP, 2, true>() : gen == 1 ? sm100_kbn<DP, 1, true>()  \
+                                                                : sm100_kbn<DP, 0, true>())  \
+              : (gen == 2 ? sm100_kbn<DP, 2, false>() : gen == 1 ? sm100_kbn<DP, 1, false>() \
+                                                                 : sm100_kbn<DP, 0, false>()))
+  return wide ? MFA_KBN(128) : MFA_KBN(64);
+#undef MFA_KBN
+}
+
 // SHORT: the one-tile, one-column-group kPack instantiation (sm100_short).
 template <int DP, bool BF16, int GEN, bool SHORT>
 int launch_sm100(const Sm100Args& args, int dev, int64_t grid, cudaStream_t st) {
@@ -400,7 +420,8 @@ int launch_sm100(const Sm100Args& args, int dev, int64_t grid, cudaStream_t st) 
   constexpr int TILES = SHORT ? 1 : sm100_tiles<DP, GEN>();
   auto k = fa_fwd_sm100<DP, BF16, GEN, CG, TILES, SHORT>;
   using R = sm100::Roles<CG, TILES>;
-  const int smem = (int)sm100::Cfg<DP, TILES>::SMEM;
+  constexpr int KBN = sm100::BlockKeys<DP, GEN, CG, TILES, SHORT>::value;
+  const int smem = (int)sm100::Cfg<DP, TILES, KBN>::SMEM;
   // The kernel re-splits its registers with setmaxnreg assuming exactly kLaunchRegs per thread
   // at launch; a build that launched with fewer would make setmaxnreg.inc wait forever.
   static std::atomic<int> launch_regs{-1};
@@ -455,8 +476,12 @@ int run_sm100(const mfa_fwd_params* p, FwdArgs a, int dev, cudaStream_t st,
   const int Bm = varlen ? 1 : p->B;
   int rc;
   if ((rc = make_map(&args.tq, p->q, p->dtype, p->D, p->Hq, Sq, Bm, p->q_stride)) != MFA_OK) return rc;
-  if ((rc = make_map(&args.tk, p->k, p->dtype, p->D, p->Hkv, Sk, Bm, p->k_stride)) != MFA_OK) return rc;
-  if ((rc = make_map(&args.tv, p->v, p->dtype, p->D, p->Hkv, Sk, Bm, p->v_stride)) != MFA_OK) return rc;
+  // K / V boxes are one block of keys of the instantiation that will run
+  const int kbn = sm100_kbn_rt(p->D > 64, sm100_gen(p), sm100_short(p));
+  if ((rc = make_map(&args.tk, p->k, p->dtype, p->D, p->Hkv, Sk, Bm, p->k_stride, 1, kbn)) != MFA_OK)
+    return rc;
+  if ((rc = make_map(&args.tv, p->v, p->dtype, p->D, p->Hkv, Sk, Bm, p->v_stride, 1, kbn)) != MFA_OK)
+    return rc;
   const int gen = sm100_gen(p);
   const bool wide = p->D > 64;
   const bool short_rows = sm100_short(p);
