@@ -154,11 +154,6 @@ def _patched(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False, 
                    is_causal=is_causal, scale=scale, **kwargs)
 
 
-def _original():
-    """The unpatched op (for callers and tests that compare against it)."""
-    return _g.orig
-
-
 def __getattr__(name):  # ``sdpa._orig`` as in the reference's module
     if name == "_orig":
         return _g.orig

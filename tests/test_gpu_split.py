@@ -206,3 +206,28 @@ def test_varlen_split_with_understated_lq_reports_instead_of_writing_past_worksp
         _kernel.check_device_errors(DEV)
     assert ei.value.status == _lib.ERR_INVALID
     assert torch.equal(ws[need:], guard)  # nothing written past the planned workspace
+
+
+@pytest.mark.parametrize("lens,kw", [
+    ([6040, 3336, 945, 4133, 1, 0, 7422, 257], dict(causal=True)),
+    ([1, 2, 1, 3, 1], dict(causal=True)),  # decode-like: packed heads and a key split
+    ([700, 1300, 90], dict(window_size=(200, 0), softcap=20.0)),
+])
+def test_varlen_exact_cta_list_matches_padded_grid(lens, kw):
+    """The exact, longest-first CTA list (host cu_seqlens known) computes every row exactly as
+    the padded grid with early-exit CTAs does: each CTA's rows, keys and order of work are the
+    same, only the CTAs' order in the grid differs, so the outputs are bitwise equal."""
+    lk = [max(n, 1) * 3 for n in lens]
+    q, k, v, cu_q, cu_k = ref.make_varlen(lens, lk, 16, 4, 128, torch.bfloat16, seed=len(lens))
+    qd, kd, vd, cqd, ckd = (t.to(DEV) for t in (q, k, v, cu_q, cu_k))
+    bias = _kernel._BiasParams(kw.get("softcap", 0.0), *kw.get("window_size", (-1, -1)), None)
+    outs = []
+    for host in (None, cu_q.tolist()):
+        o = torch.empty_like(qd)
+        _kernel.forward_varlen(qd, kd, vd, o, cqd, ckd, max(lens), max(lk), 1 / math.sqrt(128),
+                               kw.get("causal", False), bias, cu_q_host=host)
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    want = ref.flash_attn_varlen_func(q, k, v, cu_q, cu_k, **kw)
+    torch.testing.assert_close(outs[1].float().cpu(), want, **TOL[torch.bfloat16])
