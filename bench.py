@@ -9,10 +9,11 @@ the whole problem over inputs already resident in HBM (``value``). With N ranks 
 sharded over the ranks (KV-group-aligned, no communication): strong scaling, ``value`` = the
 whole problem's FLOPs over the max-over-ranks device time. At N > 1 the same line carries a
 ``split_kv`` leg: every rank holds one contiguous key range of all heads with equal causal
-work and computes partials for every query row; the forward scatters each partial row into the
-receive buffer of the rank that owns it (peer stores over NVLink) and each rank merges its own
-rows locally. The same leg with the NCCL merge (all-gather of the row log-sum-exp, rescale
-kernel, reduce-scatter by query rows) is reported beside it. Phases are timed with CUDA
+work and computes partials for every query row into its own buffer; each rank then merges its
+own rows reading every rank's partials over NVLink (peer loads, one kernel). The same leg with
+the forward pushing rows to their owners (``push_merge``) and with the NCCL merge (all-gather
+of the row log-sum-exp, rescale kernel, reduce-scatter by query rows; ``nccl_merge``) is
+reported beside it. Phases are timed with CUDA
 events. Every run checks sampled row windows of its
 output against a single-GPU forward of the same rows (``parity``).
 
@@ -349,9 +350,11 @@ def split_kv_leg(steps, warmup, dev, rank, world, flush, stream, dist, merge):
     """Config 5 as split-KV over the ranks: rank g holds one contiguous key range of all heads
     with equal causal work (balanced_ranges; all ranks draw the same seeded q/k/v on the
     device), computes partials for all 131072 query rows, and the merge leaves each rank its
-    own rows. merge = "peer": the forward scatters partial rows into their owners' receive
-    buffers over NVLink, then one local merge kernel; "nccl": all-gather of the row
-    log-sum-exp, rescale kernel, reduce-scatter. Per step, CUDA events on the launching stream
+    own rows. merge = "pull": each rank's forward writes its partials to its own buffer and
+    each rank merges its rows reading all ranks' buffers over NVLink (one kernel); "peer": the
+    forward scatters partial rows into their owners' receive buffers over NVLink, then one
+    local merge kernel; "nccl": all-gather of the row log-sum-exp, rescale kernel,
+    reduce-scatter. Per step, CUDA events on the launching stream
     time the phases; every figure is the max over ranks."""
     from mtlflashattn_b200 import distributed as mfd
 
@@ -388,9 +391,9 @@ def split_kv_leg(steps, warmup, dev, rank, world, flush, stream, dist, merge):
     for s, e, ev in parts:
         fwd = ev["forward_done"]
         ph = {"total": s.elapsed_time(e), "forward": s.elapsed_time(fwd)}
-        if merge == "peer":
+        if merge in ("peer", "pull"):
             ph["exchange_wait"] = fwd.elapsed_time(ev["exchange_done"])
-            ph["local_merge"] = ev["exchange_done"].elapsed_time(e)
+            ph["merge"] = ev["exchange_done"].elapsed_time(e)
         else:
             ph["lse_allgather"] = ev["lse_gather"][0].elapsed_time(ev["lse_gather"][1])
             ph["rescale"] = ev["lse_gather"][1].elapsed_time(ev["reduce_scatter"][0])
@@ -519,7 +522,7 @@ def run_gpu(args):
     split_failed = False
     if world > 1 and args.config == "5" and not args.no_split_kv:
         # the headline is already measured: a failure here is reported in the line, not raised
-        for merge in ("peer", "nccl"):
+        for merge in ("pull", "peer", "nccl"):
             torch.cuda.empty_cache()
             try:
                 leg = split_kv_leg(min(args.steps, args.split_steps), args.warmup, dev, rank,
@@ -530,7 +533,7 @@ def run_gpu(args):
             if split is None:
                 split = leg
             else:
-                split["nccl_merge"] = leg
+                split["push_merge" if merge == "peer" else "nccl_merge"] = leg
             if split_failed:
                 break
         torch.cuda.empty_cache()

@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define MFA_ABI_VERSION 7
+#define MFA_ABI_VERSION 8
 
 /* Status codes. The Python layer maps them to the reference's exception types. */
 enum mfa_status {
@@ -197,6 +197,16 @@ int mfa_fwd_scatter(const mfa_fwd_params* p, const mfa_peer_scatter* s, void* cu
  * Writes o [rows][H][D] in o_dtype and, if lse != NULL, lse [H][rows]. */
 int mfa_lse_merge(const float* o_parts, const float* lse_parts, int32_t n, int32_t rows,
                   int32_t H, int32_t D, void* o, int32_t o_dtype, float* lse, void* cuda_stream);
+
+/* The pull side of a split-KV over GPUs (no counterpart in the reference): each GPU has run
+ * its forward over its keys into its own fp32 partial buffer [rows_total][H][D] with row
+ * log-sum-exp [H][rows_total] (an ordinary mfa_fwd with o_dtype fp32 and lse); after all have
+ * finished, every GPU merges ITS rows [row0, row0 + nrows) from all n partials, reading the
+ * other GPUs' buffers through peer mappings (mfa_peer_open) with plain loads over NVLink.
+ * Writes o [nrows][H][D] in o_dtype and, if lse != NULL, lse [H][nrows]. */
+int mfa_lse_merge_rows(const float* const* o_parts, const float* const* lse_parts, int32_t n,
+                       int32_t rows_total, int32_t row0, int32_t nrows, int32_t H, int32_t D,
+                       void* o, int32_t o_dtype, float* lse, void* cuda_stream);
 
 /* Receive buffers for mfa_fwd_scatter: device memory on the current GPU plus its CUDA IPC
  * handle (MFA_IPC_HANDLE_BYTES bytes written to ipc_handle). */

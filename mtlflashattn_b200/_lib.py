@@ -13,7 +13,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmfa.so")
 
-MFA_ABI_VERSION = 7
+MFA_ABI_VERSION = 8
 
 # mfa_status
 OK = 0
@@ -46,6 +46,7 @@ EXPORTED_SYMBOLS = (
     "mfa_lse_rescale_sum",
     "mfa_fwd_scatter",
     "mfa_lse_merge",
+    "mfa_lse_merge_rows",
     "mfa_peer_alloc",
     "mfa_peer_open",
     "mfa_peer_close",
@@ -198,6 +199,11 @@ def load(path: str | None = None) -> ctypes.CDLL:
                                       ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
                                       ctypes.c_void_p]
         lib.mfa_lse_merge.restype = ctypes.c_int
+        lib.mfa_lse_merge_rows.argtypes = [
+            ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32,
+            ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+            ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]
+        lib.mfa_lse_merge_rows.restype = ctypes.c_int
         lib.mfa_peer_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p),
                                        ctypes.c_void_p]
         lib.mfa_peer_alloc.restype = ctypes.c_int
@@ -310,3 +316,12 @@ def peer_close(ptr: int) -> int:
 
 def peer_free(ptr: int) -> int:
     return load().mfa_peer_free(ptr)
+
+
+def lse_merge_rows(o_ptrs, lse_ptrs, rows_total, row0, nrows, H, D, o_ptr, o_dtype, lse_ptr,
+                   stream) -> int:
+    n = len(o_ptrs)
+    oa = (ctypes.c_void_p * n)(*o_ptrs)
+    la = (ctypes.c_void_p * n)(*lse_ptrs)
+    return load().mfa_lse_merge_rows(oa, la, n, rows_total, row0, nrows, H, D, o_ptr, o_dtype,
+                                     lse_ptr or None, stream)

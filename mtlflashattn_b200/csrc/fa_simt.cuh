@@ -174,6 +174,73 @@ __global__ void lse_merge_kernel(const float* __restrict__ parts, const float* _
   if (lane == 0 && lse_out != nullptr) lse_out[li] = lse;
 }
 
+// Merge of a row window from partials held by several GPUs (the pull side of a split-KV over
+// GPUs): partial g is fp32 [rows_total][H][D] at pp.o[g] (a peer-mapped pointer when another GPU
+// holds it) with its row log-sum-exp [H][rows_total] at pp.lse[g]. Rows [row0, row0 + nrows)
+// are merged into o [nrows][H][D] (TO) and optionally lse_out [H][nrows]. Plain loads, one warp
+// per (row, head), four consecutive columns per lane when vec4.
+template <typename TO>
+__global__ void lse_merge_rows_kernel(const __grid_constant__ PartPtrs pp, int n, int rows_total,
+                                      int row0, int nrows, int H, int D, TO* o, float* lse_out,
+                                      int vec4) {
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (int64_t)nrows * H) return;
+  const int r = (int)(w / H), h = (int)(w % H);
+  const int64_t li = (int64_t)h * rows_total + row0 + r;
+  const int64_t si = ((int64_t)(row0 + r) * H + h) * D;
+  const int64_t oi = ((int64_t)r * H + h) * D;
+  float lg[kMaxParts];
+  float mx = -INFINITY;
+  for (int g = 0; g < n; ++g) {
+    lg[g] = pp.lse[g][li];
+    mx = fmaxf(mx, lg[g]);
+  }
+  float tot = 0.f;
+  if (mx != -INFINITY)
+    for (int g = 0; g < n; ++g)
+      if (lg[g] != -INFINITY) tot += expf(lg[g] - mx);
+  const float inv = mx == -INFINITY ? 0.f : 1.f / tot;
+  for (int g = 0; g < n; ++g) lg[g] = (lg[g] == -INFINITY || mx == -INFINITY) ? 0.f : expf(lg[g] - mx) * inv;
+  auto put = [&](int d, float v) {
+    if constexpr (sizeof(TO) == 4) {
+      o[oi + d] = v;
+    } else {
+      o[oi + d] = TO(v);
+    }
+  };
+  if (vec4) {
+    for (int c = 4 * lane; c < D; c += 128) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int g = 0; g < n; ++g) {
+        if (lg[g] == 0.f) continue;  // a partial that saw no key of this row
+        const float4 x = *reinterpret_cast<const float4*>(pp.o[g] + si + c);
+        acc.x = fmaf(lg[g], x.x, acc.x);
+        acc.y = fmaf(lg[g], x.y, acc.y);
+        acc.z = fmaf(lg[g], x.z, acc.z);
+        acc.w = fmaf(lg[g], x.w, acc.w);
+      }
+      if constexpr (sizeof(TO) == 4) {
+        *reinterpret_cast<float4*>(o + oi + c) = acc;
+      } else {
+        put(c, acc.x);
+        put(c + 1, acc.y);
+        put(c + 2, acc.z);
+        put(c + 3, acc.w);
+      }
+    }
+  } else {
+    for (int d = lane; d < D; d += 32) {
+      float acc = 0.f;
+      for (int g = 0; g < n; ++g)
+        if (lg[g] != 0.f) acc = fmaf(lg[g], pp.o[g][si + d], acc);
+      put(d, acc);
+    }
+  }
+  if (lane == 0 && lse_out != nullptr)
+    lse_out[(int64_t)h * nrows + r] = mx == -INFINITY ? -INFINITY : mx + logf(tot);
+}
+
 // Merge of the key splits of one launch (dense layout): partial outputs ws_o fp32
 // [split][B][Lq][Hq][D] normalised by their own sums, row log-sum-exp ws_lse [split][B][Hq][Lq].
 // One block of kCombineThreads per (batch, head, row). The split weights exp(lse_s - max) are

@@ -904,4 +904,41 @@ int mfa_peer_free(void* ptr) {
   return cudaFree(ptr) == cudaSuccess ? MFA_OK : MFA_ERR_CUDA;
 }
 
+int mfa_lse_merge_rows(const float* const* o_parts, const float* const* lse_parts, int32_t n,
+                       int32_t rows_total, int32_t row0, int32_t nrows, int32_t H, int32_t D,
+                       void* o, int32_t o_dtype, float* lse, void* stream) {
+  if (mfa::fault_injected("combine")) return MFA_ERR_FAULT_INJECTED;
+  mfa::NvtxRange range("mfa_lse_merge_rows");
+  if (n < 1 || n > mfa::kMaxParts || rows_total < 0 || row0 < 0 || nrows < 0 ||
+      (int64_t)row0 + nrows > rows_total || H < 1 || D < 1 || o_dtype < 0 || o_dtype > 2)
+    return MFA_ERR_INVALID;
+  if (nrows == 0) return MFA_OK;
+  if (o_parts == nullptr || lse_parts == nullptr || o == nullptr) return MFA_ERR_INVALID;
+  mfa::PartPtrs pp;
+  std::memset(&pp, 0, sizeof(pp));
+  bool vec4 = D % 4 == 0 && mfa::aligned16(o);
+  for (int g = 0; g < n; ++g) {
+    if (o_parts[g] == nullptr || lse_parts[g] == nullptr) return MFA_ERR_INVALID;
+    pp.o[g] = o_parts[g];
+    pp.lse[g] = lse_parts[g];
+    vec4 = vec4 && mfa::aligned16(o_parts[g]);
+  }
+  const int64_t blocks = ((int64_t)nrows * H * 32 + 255) / 256;
+  if (blocks >= (1ll << 31)) return MFA_ERR_UNSUPPORTED;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  (void)cudaGetLastError();
+  const unsigned nb = (unsigned)blocks;
+  const int v4 = vec4 ? 1 : 0;
+  if (o_dtype == MFA_FP32)
+    mfa::lse_merge_rows_kernel<float><<<nb, 256, 0, st>>>(pp, n, rows_total, row0, nrows, H, D,
+                                                           (float*)o, lse, v4);
+  else if (o_dtype == MFA_BF16)
+    mfa::lse_merge_rows_kernel<__nv_bfloat16><<<nb, 256, 0, st>>>(
+        pp, n, rows_total, row0, nrows, H, D, (__nv_bfloat16*)o, lse, v4);
+  else
+    mfa::lse_merge_rows_kernel<__half><<<nb, 256, 0, st>>>(pp, n, rows_total, row0, nrows, H, D,
+                                                            (__half*)o, lse, v4);
+  return cudaGetLastError() == cudaSuccess ? MFA_OK : MFA_ERR_CUDA;
+}
+
 }  // extern "C"

@@ -24,14 +24,23 @@ Two decompositions, neither present in the reference (its tiers run on one Apple
   The rank's key chunks are launches of the forward kernel writing their partials straight
   into the row-major layout (output strides), so no transpose or eager merge runs over them.
 
-* Split-KV merged through peer memory (``merge="peer"``, the default on CUDA). The forward
+* Split-KV merged by pulling through peer memory (``merge="pull"``, the default on CUDA).
+  Each rank's forward writes its partial rows and log-sum-exp into its own buffer (local
+  stores at full speed; the buffer is libmfa-allocated so it carries a CUDA IPC handle and is
+  mapped on every other rank). After an ordering point, each rank merges its own rows with one
+  kernel (``mfa_lse_merge_rows``) that reads the rows from every rank's buffer with plain loads
+  over NVLink and writes the final rows in the output dtype.
+
+* Split-KV merged by pushing through peer memory (``merge="peer"``). The forward
   kernel's epilogue stores every partial row directly into the receive buffer of the GPU that
   owns the row (``mfa_fwd_scatter``: plain stores over NVLink into buffers mapped with CUDA
   IPC), so the exchange runs while the attention runs, tile by tile; each GPU then merges its
   own rows with one local kernel (``mfa_lse_merge``) that writes the final rows in the output
-  dtype. No all-gather, rescale pass or reduce-scatter remains. Ordering between GPUs comes
-  from two one-element NCCL all-reduces per call (receive buffers free before the scatter, all
-  partial rows landed before the merge); no kernel ever waits on another GPU. With
+  dtype. No all-gather, rescale pass or reduce-scatter remains. On 4 GPUs the remote stores
+  slowed the forward by ~19 % (3/4 of the rows are remote), which is why pulling is the default.
+  For both, ordering between GPUs comes from two one-element NCCL all-reduces per call (buffers
+  free before they are written, all partial rows written before they are read); no kernel ever
+  waits on another GPU. With
   ``balanced_ranges`` each rank holds ONE contiguous key range of equal causal work, so a
   rank makes one launch and each row has one partial per rank.
 
@@ -212,8 +221,8 @@ class _PeerBuffers:
         self.sync = torch.zeros(1, device=device)
 
     @classmethod
-    def get(cls, group, slots, rows_per, BH, D, device):
-        key = (id(group), dist.get_world_size(group), slots, rows_per, BH, D, str(device))
+    def get(cls, group, slots, rows_per, BH, D, device, kind="push"):
+        key = (kind, id(group), dist.get_world_size(group), slots, rows_per, BH, D, str(device))
         buf = cls._cache.get(key)
         if buf is None:
             buf = cls._cache[key] = cls(group, slots, rows_per, BH, D, device)
@@ -226,6 +235,19 @@ class _PeerBuffers:
             sc.o_recv[g] = self.base[g]
             sc.lse_recv[g] = self.base[g] + self.o_bytes
         return sc
+
+
+class _DeviceArray:
+    """A device pointer presented as an array (``__cuda_array_interface__``), so torch can view
+    memory libmfa allocated without copying it."""
+
+    def __init__(self, ptr, shape, typestr="<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 2}
+
+
+def _view(ptr, shape, device):
+    return torch.as_tensor(_DeviceArray(ptr, shape), device=device)
 
 
 def _order(buf, group):
@@ -271,6 +293,45 @@ def _split_kv_peer(q, k_parts, v_parts, key_ranges, lk_total, scale, causal, bia
     return out[: r1 - r0].transpose(0, 1), (r0, r1)
 
 
+def _split_kv_pull(q, k_parts, v_parts, key_ranges, lk_total, scale, causal, bias, group,
+                   out_dtype, events):
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    B, Lq, Hq, D = q.shape
+    nch = len(k_parts)
+    BH = B * Hq
+    buf = _PeerBuffers.get(group, nch, Lq, BH, D, q.device, kind="pull")
+    slot_o = Lq * BH * D * 4
+    slot_lse = BH * Lq * 4
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    _order(buf, group)  # every rank has finished reading this rank's buffer in the last call
+    own = buf.base[rank]
+    for c, (kp, vp, (a, _)) in enumerate(zip(k_parts, v_parts, key_ranges)):
+        # this rank's partial rows, row-major [Lq][B][Hq][D] fp32, and their log-sum-exp
+        o = _view(own + c * slot_o, (Lq, B, Hq, D), q.device)
+        lse = _view(own + buf.o_bytes + c * slot_lse, (B, Hq, Lq), q.device)
+        _kernel.forward_bshd(q, kp, vp, o.transpose(0, 1), scale, causal, bias, lse=lse,
+                             k_pos_offset=a, lk_total=lk_total)
+    if events is not None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        events["forward_done"] = ev
+    _order(buf, group)  # every rank's partials are complete
+    if events is not None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        events["exchange_done"] = ev
+    r0, r1 = row_shard(Lq, world, rank)
+    out = torch.empty(max(r1 - r0, 0), B, Hq, D, device=q.device, dtype=out_dtype)
+    o_ptrs = [buf.base[g] + c * slot_o for g in range(world) for c in range(nch)]
+    lse_ptrs = [buf.base[g] + buf.o_bytes + c * slot_lse for g in range(world) for c in range(nch)]
+    rc = _lib.lse_merge_rows(o_ptrs, lse_ptrs, Lq, r0, r1 - r0, BH, D, out.data_ptr(),
+                             _kernel._DTYPES[out_dtype], None, stream)
+    if rc != _lib.OK:
+        _kernel._raise_status(rc, "mfa_lse_merge_rows")
+    return out.transpose(0, 1), (r0, r1)
+
+
 def flash_attn_split_kv(q, k_parts, v_parts, key_ranges, lk_total, softmax_scale=None,
                         causal=False, window_size=(-1, -1), softcap=0.0, alibi_slopes=None,
                         group=None, out_dtype=None, gather=False, events=None, merge="auto"):
@@ -282,11 +343,12 @@ def flash_attn_split_kv(q, k_parts, v_parts, key_ranges, lk_total, softmax_scale
     query rows of the merged output. With ``gather=True`` the rows of every rank are
     all-gathered and the full [B, Lq, Hq, D] output is returned on every rank instead.
 
-    ``merge``: "peer" (partial rows scattered to their owners through peer memory by the
-    forward itself, then merged locally), "nccl" (all-gather of the row log-sum-exp, rescale,
-    reduce-scatter), or "auto": "peer" when the tensor-core kernel takes the inputs and the
-    group has at most 8 ranks, else "nccl". With "peer" every rank must pass the same number of
-    key chunks (each chunk has its slot in the receive buffers)."""
+    ``merge``: "pull" (each rank's forward writes its partials to its own buffer; each rank
+    then merges its rows reading every rank's buffer through peer memory), "peer" (the forward
+    scatters partial rows to their owners through peer memory, then a local merge), "nccl"
+    (all-gather of the row log-sum-exp, rescale, reduce-scatter), or "auto": "pull" when the
+    tensor-core kernel takes the inputs and the group has at most 8 ranks, else "nccl". With
+    "pull" and "peer" every rank must pass the same number of key chunks."""
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q.shape[-1])
     B, Lq, Hq, D = q.shape
     alibi = (_kernel._broadcast_alibi_slopes(alibi_slopes, B, Hq, q.device)
@@ -296,7 +358,11 @@ def flash_attn_split_kv(q, k_parts, v_parts, key_ranges, lk_total, softmax_scale
     if merge == "auto":
         peer_ok = (q.is_cuda and world <= _lib.MAX_PEERS and q.shape[-1] % 8 == 0
                    and q.dtype in (torch.float16, torch.bfloat16))
-        merge = "peer" if peer_ok else "nccl"
+        merge = "pull" if peer_ok else "nccl"
+    if merge == "pull":
+        out, rows = _split_kv_pull(q, k_parts, v_parts, key_ranges, lk_total, scale, causal,
+                                   bias, group, out_dtype or q.dtype, events)
+        return _gather_rows(out, rows, Lq, group) if gather else (out, rows)
     if merge == "peer":
         out, rows = _split_kv_peer(q, k_parts, v_parts, key_ranges, lk_total, scale, causal,
                                    bias, group, out_dtype or q.dtype, events)

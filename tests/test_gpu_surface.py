@@ -214,15 +214,16 @@ def test_lse_rescale_sum_kernel_matches_torch():
 
 @pytest.mark.parametrize("ranges", [[(0, 300), (300, 1000)], [(0, 1000)]])
 def test_split_kv_peer_merge_single_rank(nccl_single_rank, ranges):
-    """The peer-memory merge on one rank: the forward scatters its partial rows into the
-    (local) receive buffer, one slot per key chunk, and mfa_lse_merge combines the slots;
-    checked against the oracle and against the NCCL merge."""
+    """The peer-memory merges on one rank: "peer" scatters partial rows from the forward into
+    the (local) receive buffer, one slot per key chunk, and mfa_lse_merge combines the slots;
+    "pull" writes the partials to the rank's own buffer and mfa_lse_merge_rows merges its rows
+    through the peer pointers; checked against the oracle and against the NCCL merge."""
     q, k, v = ref.make_qkv(1, 700, 1000, 4, 2, 128, torch.bfloat16, seed=13)
     qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
     kp, vp = [kd[:, a:b] for a, b in ranges], [vd[:, a:b] for a, b in ranges]
     want = ref.flash_attn_func(q, k, v, causal=True, window_size=(500, -1))
     outs = {}
-    for merge in ("peer", "nccl"):
+    for merge in ("pull", "peer", "nccl"):
         for _ in range(2):  # the second call reuses the receive buffers
             out, rows = mfd.flash_attn_split_kv(qd, kp, vp, ranges, 1000, causal=True,
                                                 window_size=(500, -1), merge=merge)
@@ -230,6 +231,7 @@ def test_split_kv_peer_merge_single_rank(nccl_single_rank, ranges):
         torch.testing.assert_close(out.float().cpu(), want, atol=2e-2, rtol=2e-2)
         outs[merge] = out.float()
     torch.testing.assert_close(outs["peer"], outs["nccl"], atol=8e-3, rtol=1e-2)
+    torch.testing.assert_close(outs["pull"], outs["peer"], atol=8e-3, rtol=1e-2)
 
 
 def test_lse_merge_kernel_matches_torch():

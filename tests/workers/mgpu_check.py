@@ -35,8 +35,9 @@ parts = [torch.empty_like(loc) for _ in range(world)]
 dist.all_gather(parts, loc.contiguous())
 assert torch.equal(g, torch.cat(parts, dim=2))
 msgs = []
+balanced = lambda L_, w, r: mfd.balanced_ranges(L_, w, r, causal=True)  # noqa: E731
 for ranges_of, merge in ((mfd.zigzag_ranges, "nccl"), (mfd.zigzag_ranges, "peer"),
-                         (lambda L_, w, r: mfd.balanced_ranges(L_, w, r, causal=True), "peer")):
+                         (mfd.zigzag_ranges, "pull"), (balanced, "peer"), (balanced, "pull")):
     rng = ranges_of(L, world, rank)
     kp, vp = [kd[:, a:b] for a, b in rng], [vd[:, a:b] for a, b in rng]
     for _ in range(2):  # a second call reuses the peer receive buffers
