@@ -3,8 +3,8 @@
 // pointers that TMA cannot address. It reads q/k/v through arbitrary (batch, seq, head) strides,
 // so no layout copy is ever made.
 //
-// CTA = 128 threads = 32 query rows x 4 threads per row; keys stream in blocks of 16 through
-// shared memory. Online softmax in fp32 with expf; semantics of the reference's chunked-fp32
+// CTA = 128 threads = 32 query rows x 4 threads per row (or 8 rows x 16 threads for small
+// launches); keys stream in blocks of 16 through shared memory. Online softmax in fp32 with expf; semantics of the reference's chunked-fp32
 // tier (metal_flash_attn/_kernel.py:1165-1208) and of its scalar v0 kernel (_kernel.py:32-87).
 #pragma once
 #include "common.cuh"
@@ -12,9 +12,12 @@
 
 namespace mfa {
 namespace simt {
-constexpr int BM = 32;
 constexpr int BN = 16;
 constexpr int kThreads = 128;
+// TPR threads share a query row: 4 (32 rows per CTA) normally, 16 (8 rows per CTA) when a
+// launch would otherwise leave SMs idle, so small problems get four times the CTAs.
+template <int TPR>
+__host__ __device__ constexpr int rows_per_cta() { return kThreads / TPR; }
 }  // namespace simt
 
 template <typename T>
@@ -28,10 +31,12 @@ __device__ __forceinline__ void store_elem(const FwdArgs& a, void* row_ptr, int 
   }
 }
 
-template <typename T, int DP>
+template <typename T, int DP, int TPR = 4>
 __global__ void __launch_bounds__(simt::kThreads) fa_fwd_simt(const __grid_constant__ FwdArgs a) {
   using namespace simt;
-  constexpr int NC = DP / 4;  // output columns per thread
+  static_assert(TPR == 4 || TPR == 16, "threads per row");
+  constexpr int BM = rows_per_cta<TPR>();
+  constexpr int NC = DP / TPR;  // output columns per thread
   __shared__ float sQ[BM][DP + 1];
   __shared__ float sK[BN][DP + 1];
   __shared__ float sV[BN][DP];
@@ -52,8 +57,8 @@ __global__ void __launch_bounds__(simt::kThreads) fa_fwd_simt(const __grid_const
   const T* kp = reinterpret_cast<const T*>(a.k);
   const T* vp = reinterpret_cast<const T*>(a.v);
   const int tid = threadIdx.x;
-  const int r = tid >> 2;
-  const int sub = tid & 3;
+  const int r = tid / TPR;
+  const int sub = tid % TPR;
   const int64_t row = (int64_t)r0 + r;
   const int D = a.D;
 
@@ -93,11 +98,11 @@ __global__ void __launch_bounds__(simt::kThreads) fa_fwd_simt(const __grid_const
     }
     __syncthreads();
 
-    float s[BN / 4];
+    float s[BN / TPR];
     float mx = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < BN / 4; ++i) {
-      const int kk = sub + 4 * i;
+    for (int i = 0; i < BN / TPR; ++i) {
+      const int kk = sub + TPR * i;
       float dot = 0.f;
 #pragma unroll 8
       for (int d = 0; d < DP; ++d) dot = fmaf(sQ[r][d], sK[kk][d], dot);
@@ -108,25 +113,25 @@ __global__ void __launch_bounds__(simt::kThreads) fa_fwd_simt(const __grid_const
       s[i] = (key >= kr.lo && key < kr.hi) ? val : -INFINITY;
       mx = fmaxf(mx, s[i]);
     }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+#pragma unroll
+    for (int o = 1; o < TPR; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     const float m_new = fmaxf(m, mx);
     float corr = 1.f;
     float ls = 0.f;
     if (m_new != -INFINITY) {
       corr = (m == -INFINITY) ? 0.f : expf(m - m_new);
 #pragma unroll
-      for (int i = 0; i < BN / 4; ++i) {
+      for (int i = 0; i < BN / TPR; ++i) {
         const float p = (s[i] == -INFINITY) ? 0.f : expf(s[i] - m_new);
-        sP[r][sub + 4 * i] = p;
+        sP[r][sub + TPR * i] = p;
         ls += p;
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < BN / 4; ++i) sP[r][sub + 4 * i] = 0.f;
+      for (int i = 0; i < BN / TPR; ++i) sP[r][sub + TPR * i] = 0.f;
     }
-    ls += __shfl_xor_sync(0xffffffffu, ls, 1);
-    ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+#pragma unroll
+    for (int o = 1; o < TPR; o <<= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
     l = l * corr + ls;
     m = m_new;
     __syncwarp();
@@ -136,7 +141,7 @@ __global__ void __launch_bounds__(simt::kThreads) fa_fwd_simt(const __grid_const
     for (int kk = 0; kk < BN; ++kk) {
       const float p = sP[r][kk];
 #pragma unroll
-      for (int c = 0; c < NC; ++c) acc[c] = fmaf(p, sV[kk][sub + 4 * c], acc[c]);
+      for (int c = 0; c < NC; ++c) acc[c] = fmaf(p, sV[kk][sub + TPR * c], acc[c]);
     }
   }
 
@@ -147,7 +152,7 @@ __global__ void __launch_bounds__(simt::kThreads) fa_fwd_simt(const __grid_const
                     esz * ((int64_t)sv.qb * a.o_sb + (int64_t)(sv.q0 + row) * a.o_ss + (int64_t)h * a.o_sh);
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
-      const int d = sub + 4 * c;
+      const int d = sub + TPR * c;
       if (d < D) store_elem<T>(a, orow, d, acc[c] * inv);
     }
     if (sub == 0 && a.lse != nullptr)
