@@ -268,10 +268,9 @@ def run_reference(args):
         return 0
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    # size the per-step sample so the whole --steps/--warmup run stays within ~2 minutes
-    _, t256, _ = cpu_sample_run(steps=1, rows=256)
-    budget = 120.0 / max(1, args.steps + args.warmup)
-    rows = int(max(16, min(1024, 256 * budget / max(t256, 1e-6))) // 16 * 16)
+    # a fixed sample (the same 256 middle rows the GPU line's cpu_baseline uses), so the work per
+    # step does not depend on the host: ~0.1 s per step on 16 cores
+    rows = 256
     for _ in range(args.warmup):
         cpu_sample_run(steps=1, rows=rows)
     tf, t, desc = cpu_sample_run(steps=args.steps, rows=rows)
